@@ -1,0 +1,558 @@
+"""Benchmark of the B200 paged-decode attention (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (N = 1): BASELINE config 2 -- Qwen2.5-3B decode attention, B=8,
+16 query / 2 KV heads, head_dim 128, block_size 32, context 2048, bf16, KV
+pool 2x the needed blocks with scattered block tables.  A step is one
+decode-attention call over the batch (one kernel launch).  Inputs rotate over
+12 independent KV pools (403 MB > 3x the 126 MB L2) so HBM, not L2, is
+measured.  The timed K steps run as CUDA-graph replays of the public API's
+launch; time is taken with CUDA events on the launching stream.
+
+With N > 1 (torchrun, one rank per GPU) every rank runs the same per-GPU
+workload on its own requests (requests are independent: no data-path
+collective), ``scaling`` is "weak" and ``value`` is the whole-job tokens/s
+(N * B * K / max-over-ranks time).  The nested ``ragged`` object reports
+BASELINE config 4 (B=64 Llama-3-8B shape, log-uniform lengths up to 131072)
+sharded across the N ranks by length-balanced (LPT) request sharding.
+
+``--impl reference`` times the reference algorithm on the host CPU (the numpy
+oracle that restates flashdec/paged_reference.py) on the same workload, on
+rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = ("paged decode attn p50 µs & HBM GB/s (% of peak), B8 ctx2048; "
+          "tok/s at 1–8 GPUs")
+C2 = dict(batch=8, hq=16, hkv=2, d=128, bs=32, ctx=2048, pool_factor=2)
+NUM_POOLS = 12
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_from_profile(name):
+    """Per-launch DRAM bytes recorded by an ncu capture (profiles/<name>.txt)."""
+    p = REPO / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def build_c2_pools(torch, device, seed):
+    cfg = C2
+    b, hkv, d, bs = cfg["batch"], cfg["hkv"], cfg["d"], cfg["bs"]
+    nblk = cfg["ctx"] // bs
+    pool = cfg["pool_factor"] * b * nblk
+    g = torch.Generator(device=device).manual_seed(seed)
+    pools = []
+    for _ in range(NUM_POOLS):
+        k = torch.randn((pool, hkv, bs, d), device=device, dtype=torch.bfloat16, generator=g)
+        v = torch.randn((pool, hkv, bs, d), device=device, dtype=torch.bfloat16, generator=g)
+        perm = torch.randperm(pool, device=device, generator=g)[: b * nblk]
+        bt = perm.reshape(b, nblk).to(torch.int32).contiguous()
+        q = torch.randn((b, cfg["hq"], d), device=device, dtype=torch.bfloat16, generator=g)
+        pools.append(dict(q=q, k=k, v=v, bt=bt))
+    sl = torch.full((b,), cfg["ctx"], device=device, dtype=torch.int32)
+    return pools, sl
+
+
+def c2_bytes():
+    from oracle.paged_attention import attention_bytes
+
+    return attention_bytes([C2["ctx"]] * C2["batch"], C2["hq"], C2["hkv"], C2["d"], C2["bs"])
+
+
+def ragged_requests(seed=4, batch=64):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    return [int(x) for x in np.exp(rng.uniform(np.log(512), np.log(131072), size=batch))]
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import flashdec_b200
+    from flashdec_b200.sharding import lpt_partition
+    from oracle.paged_attention import attention_bytes
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    pools, sl = build_c2_pools(torch, device, seed=1234 + rank)
+    outs = [torch.empty_like(p["q"]) for p in pools]
+    stream = torch.cuda.Stream(device)
+
+    def step(i):
+        p = pools[i % NUM_POOLS]
+        flashdec_b200.paged_decode_attention_into(p["q"], p["k"], p["v"], p["bt"], sl,
+                                                  outs[i % NUM_POOLS])
+
+    # warm-up (also sizes the workspace and builds tensor maps)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+    stream.synchronize()
+
+    # graph of G steps (rotating pools), replayed to cover exactly K steps
+    G = min(args.steps, 1200)
+    G -= G % NUM_POOLS if G >= NUM_POOLS else 0
+    G = max(G, 1)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(G):
+            step(i)
+    reps, rem = divmod(args.steps, G)
+    graph_rem = None
+    if rem:
+        graph_rem = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_rem, stream=stream):
+            for i in range(rem):
+                step(i)
+    for _ in range(2):
+        graph.replay()
+    stream.synchronize()
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            if graph_rem is not None:
+                graph_rem.replay()
+            end.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_per_step = max_ms / args.steps
+
+    # p50 of single launches (one-step graphs, GPU kept busy so host enqueue
+    # time is not inside the events)
+    single = []
+    for i in range(NUM_POOLS):
+        gi = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gi, stream=stream):
+            step(i)
+        single.append(gi)
+    lat = []
+    with torch.cuda.stream(stream):
+        for r in range(240):
+            torch.cuda._sleep(20000)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            single[r % NUM_POOLS].replay()
+            e1.record(stream)
+            lat.append((e0, e1))
+    stream.synchronize()
+    lat_us = sorted(a.elapsed_time(b) * 1000.0 for a, b in lat[40:])
+    p50_us = lat_us[len(lat_us) // 2]
+
+    # end to end through the public API: pinned host inputs, H2D, decode, D2H
+    e2e = None
+    if rank == 0 or world > 1:
+        e2e_steps = min(args.steps, 3000)
+        hq = [p["q"].cpu().pin_memory() for p in pools]
+        hbt = [p["bt"].cpu().pin_memory() for p in pools]
+        hsl = sl.cpu().pin_memory()
+        hout = [torch.empty_like(p["q"], device="cpu").pin_memory() for p in pools]
+        dq = torch.empty_like(pools[0]["q"])
+        dbt = torch.empty_like(pools[0]["bt"])
+        dsl = torch.empty_like(sl)
+
+        def e2e_step(i):
+            j = i % NUM_POOLS
+            dq.copy_(hq[j], non_blocking=True)
+            dbt.copy_(hbt[j], non_blocking=True)
+            dsl.copy_(hsl, non_blocking=True)
+            o = flashdec_b200.decode(dq, pools[j]["k"], pools[j]["v"], dbt, dsl)
+            hout[j].copy_(o, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for i in range(20):
+                e2e_step(i)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for i in range(e2e_steps):
+                e2e_step(i)
+            s1.record(stream)
+        stream.synchronize()
+        wall = time.perf_counter() - t0
+        ev_ms = s0.elapsed_time(s1)
+        te = torch.tensor([max(ev_ms, wall * 1000.0)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item())
+        e2e = {
+            "value": world * C2["batch"] * e2e_steps / (e2e_ms / 1000.0),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": int(dq.numel() * dq.element_size() + dbt.numel() * 4 + dsl.numel() * 4),
+            "d2h_bytes_per_step": int(dq.numel() * dq.element_size()),
+            "steps": e2e_steps,
+            "api": "flashdec_b200.decode",
+        }
+
+    # ragged long-context batch, LPT-sharded over ranks
+    ragged = run_ragged(torch, dist, device, rank, world, stream, args)
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        return None
+    nbytes = c2_bytes()
+    peak, peak_kind = _peaks()
+    achieved = nbytes / (ms_per_step / 1000.0) / 1e9
+    cpu = cpu_baseline_sample(args)
+    return {
+        "metric": METRIC,
+        "value": world * C2["batch"] * args.steps / (max_ms / 1000.0),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "p50_us": p50_us,
+        "hbm_gbs": achieved,
+        "pct_of_peak": 100.0 * achieved / peak,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, scattered block tables)",
+        "config": {
+            "workload": "BASELINE c2: Qwen2.5-3B-shape paged decode attention, B8 ctx2048",
+            "batch_per_gpu": C2["batch"], "q_heads": C2["hq"], "kv_heads": C2["hkv"],
+            "head_dim": C2["d"], "block_size": C2["bs"], "context": C2["ctx"],
+            "kv_pool_blocks": C2["pool_factor"] * C2["batch"] * C2["ctx"] // C2["bs"],
+            "l2": f"inputs rotate over {NUM_POOLS} KV pools ({NUM_POOLS * 2 * 2 * C2['batch'] * C2['ctx'] * C2['hkv'] * C2['d'] * 2 * C2['pool_factor'] // 2**20} MiB) > 3x L2",
+            "timing": "CUDA-graph replay of the public API launch, CUDA events, max over ranks",
+            "parallelism": f"request-sharded x{world} (no data-path collective)",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": _traffic_from_profile("paged_decode_c2_ctx2048"),
+            "algorithmic_bytes_per_launch": nbytes,
+            "kernel": "fd::paged_decode_kernel<bf16,128,tma>",
+        },
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "ragged": ragged,
+        "clocks": clocks.summary(),
+    }
+
+
+def run_ragged(torch, dist, device, rank, world, stream, args):
+    """B=64 Llama-3-8B attention shape (32q/8kv, D128,
+    bs16) with log-uniform lengths in [512, 131072], LPT-sharded."""
+    import flashdec_b200
+    from flashdec_b200.sharding import lpt_partition
+    from oracle.paged_attention import attention_bytes
+
+    lens = ragged_requests()
+    shards = lpt_partition(lens, world)
+    mine = [lens[i] for i in shards[rank]]
+    hq, hkv, d, bs = 32, 8, 128, 16
+    nblk = [-(-n // bs) for n in mine]
+    total = sum(nblk)
+    g = torch.Generator(device=device).manual_seed(99 + rank)
+    k = torch.randn((total + 1, hkv, bs, d), device=device, dtype=torch.bfloat16, generator=g)
+    v = torch.randn_like(k)
+    perm = torch.randperm(total + 1, device=device, generator=g)
+    bt = torch.full((len(mine), max(nblk)), -1, device=device, dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[pos:pos + n].to(torch.int32)
+        pos += n
+    sl = torch.tensor(mine, device=device, dtype=torch.int32)
+    q = torch.randn((len(mine), hq, d), device=device, dtype=torch.bfloat16, generator=g)
+    out = torch.empty_like(q)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            flashdec_b200.paged_decode_attention_into(q, k, v, bt, sl, out)
+    stream.synchronize()
+    steps = max(5, min(args.steps // 200, 50))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        flashdec_b200.paged_decode_attention_into(q, k, v, bt, sl, out)
+    graph.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    local_bytes = attention_bytes(mine, hq, hkv, d, bs)
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    peak, _ = _peaks()
+    return {
+        "workload": "BASELINE c4: B64 Llama-3-8B attention (32q/8kv, D128, bs16), seq log-uniform [512,131072]",
+        "tokens_per_step": len(lens),
+        "ms_per_step_max_rank": max_ms,
+        "tokens_per_s": len(lens) / (max_ms / 1000.0),
+        "rank0_requests": len(mine),
+        "rank0_hbm_gbs": local_bytes / (ms / 1000.0) / 1e9,
+        "rank0_frac_of_peak": local_bytes / (ms / 1000.0) / 1e9 / peak,
+        "steps": steps,
+        "scaling": "strong (fixed 64-request batch split across ranks)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# CPU reference (the numpy oracle restating flashdec/paged_reference.py)
+# ---------------------------------------------------------------------------
+def _cpu_workload(seed=7):
+    import numpy as np
+
+    from tests.golden.cases import _normal
+
+    rng = np.random.default_rng(seed)
+    b, hq, hkv, d, bs, ctx = C2["batch"], C2["hq"], C2["hkv"], C2["d"], C2["bs"], C2["ctx"]
+    nblk = ctx // bs
+    pool = C2["pool_factor"] * b * nblk
+    q = _normal(rng, (b, hq, d), "bfloat16")
+    k = _normal(rng, (pool, hkv, bs, d), "bfloat16")
+    v = _normal(rng, (pool, hkv, bs, d), "bfloat16")
+    bt = rng.permutation(pool)[: b * nblk].reshape(b, nblk).astype(np.int32)
+    sl = np.full((b,), ctx, np.int32)
+    return q, k, v, bt, sl
+
+
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        return 1
+
+
+def cpu_baseline_sample(args, seconds=None):
+    """Time the oracle on a bounded sample of the c2 workload (sequences)."""
+    from oracle import paged_decode_attention_ref
+
+    q, k, v, bt, sl = _cpu_workload()
+    seconds = seconds if seconds is not None else float(os.environ.get("FD_CPU_SECONDS", "10"))
+    n_seq = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        i = n_seq % C2["batch"]
+        paged_decode_attention_ref(q[i:i + 1], k, v, bt[i:i + 1], sl[i:i + 1], dtype="bfloat16")
+        n_seq += 1
+    dt = time.perf_counter() - t0
+    return {
+        "value": n_seq / dt,
+        "unit": "tokens/s",
+        "cores": _blas_threads(),
+        "kind": "port",
+        "sample": f"{n_seq} sequences of the c2 workload (ctx 2048, 16q/2kv, D128) in {dt:.1f} s, "
+                  "numpy oracle restating flashdec/paged_reference.py:19-125",
+    }
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    # per step: one full c2 batch (8 sequences) through the oracle; steps are
+    # capped so the run stays within a few minutes.
+    from oracle import paged_decode_attention_ref
+
+    q, k, v, bt, sl = _cpu_workload()
+    for _ in range(max(1, min(args.warmup, 2))):
+        paged_decode_attention_ref(q, k, v, bt, sl, dtype="bfloat16")
+    budget = float(os.environ.get("FD_REF_SECONDS", "60"))
+    steps = 0
+    t0 = time.perf_counter()
+    while steps < args.steps and time.perf_counter() - t0 < budget:
+        paged_decode_attention_ref(q, k, v, bt, sl, dtype="bfloat16")
+        steps += 1
+    dt = time.perf_counter() - t0
+    value = C2["batch"] * steps / dt
+    return {
+        "metric": METRIC,
+        "impl": "reference",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "steps_requested": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * dt / steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 inputs, fp32 math",
+        "data": "synthetic (seeded N(0,1) q/k/v, scattered block tables)",
+        "config": {"workload": "BASELINE c2: Qwen2.5-3B-shape paged decode attention, B8 ctx2048",
+                   "device": "host CPU"},
+        "cpu_baseline": {
+            "value": value, "unit": "tokens/s", "cores": _blas_threads(), "kind": "port",
+            "sample": f"{steps} full c2 steps (capped at {budget:.0f} s) through the numpy "
+                      "oracle restating flashdec/paged_reference.py:19-125",
+        },
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=120000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

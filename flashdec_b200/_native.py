@@ -1,0 +1,257 @@
+"""Marshalling from torch tensors to the C-ABI structs, and workspace reuse.
+
+torch is used here only for device memory, the current stream and dtype
+codes; every launch goes through ``libflashdec_b200.so``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import threading
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.FD_DTYPE_F32, torch.float16: _lib.FD_DTYPE_F16,
+               torch.bfloat16: _lib.FD_DTYPE_BF16}
+_INDEX_CODE = {torch.int32: _lib.FD_INDEX_I32, torch.int64: _lib.FD_INDEX_I64}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    return _DTYPE_CODE[t.dtype]
+
+
+def index_code(t: torch.Tensor) -> int:
+    return _INDEX_CODE[t.dtype]
+
+
+def stream_handle(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def strides(t: torch.Tensor, n: int):
+    s = t.stride()
+    if len(s) != n:
+        raise ValueError(f"expected a rank-{n} tensor, got rank {len(s)}")
+    return s
+
+
+# --------------------------------------------------------------------------
+# workspace: a zero-filled int32 ticket array (the kernel leaves it zero) and
+# fp32 scratch, per device, grown on demand and reused by every call on that
+# device.  Calls that share it must be ordered on one stream.
+# --------------------------------------------------------------------------
+class _Workspace:
+    def __init__(self):
+        self.tickets = None
+        self.scratch = None
+
+
+_ws_lock = threading.Lock()
+_ws: dict[int, _Workspace] = {}
+
+
+def workspace(device: torch.device, tickets_needed: int, scratch_bytes: int):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _ws.setdefault(idx, _Workspace())
+        grow_t = tickets_needed > 0 and (ws.tickets is None or ws.tickets.numel() < tickets_needed)
+        grow_s = scratch_bytes > 0 and (ws.scratch is None or ws.scratch.numel() * 4 < scratch_bytes)
+        if (grow_t or grow_s) and torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(
+                "flashdec_b200 workspace must grow during CUDA graph capture; run one eager "
+                "call with the largest batch first (or call reserve_workspace)"
+            )
+        if grow_t:
+            cap = max(1024, 1 << math.ceil(math.log2(tickets_needed)))
+            ws.tickets = torch.zeros(cap, dtype=torch.int32, device=device)
+        if grow_s:
+            n = max(1 << 16, 1 << math.ceil(math.log2((scratch_bytes + 3) // 4)))
+            ws.scratch = torch.empty(n, dtype=torch.float32, device=device)
+        return ws.tickets, ws.scratch
+
+
+def reserve_workspace(device, tickets: int, scratch_bytes: int) -> None:
+    """Pre-size the per-device workspace (call before CUDA graph capture)."""
+    workspace(torch.device(device), tickets, scratch_bytes)
+
+
+# --------------------------------------------------------------------------
+# paged decode
+# --------------------------------------------------------------------------
+def paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, block_size, num_seqs,
+                 num_splits=0, epilogue=_lib.FD_EPILOGUE_FUSED, append_k=None, append_v=None,
+                 slot_mapping=None, partials=None, max_ctas=0, min_tiles_per_cta=0):
+    """Launch fd_paged_decode.
+
+    ``k4``/``v4`` are 4-D views in logical order [block, kv_head, token, dim]
+    (any strides).  ``partials`` = (acc, max, sum) in the reference split
+    workspace layout, or None for the internal workspace.
+    """
+    lib = _lib.load_library()
+    a = _lib.PagedDecodeArgs()
+    a.struct_size = ctypes.sizeof(_lib.PagedDecodeArgs)
+    a.dtype = dtype_code(q)
+    a.num_seqs = int(num_seqs)
+    a.num_q_heads = q.shape[1]
+    a.num_kv_heads = k4.shape[1]
+    a.head_dim = q.shape[2]
+    a.block_size = int(block_size)
+    a.num_blocks = k4.shape[0]
+    a.max_blocks_per_seq = block_tables.shape[1]
+    a.sm_scale = float(sm_scale)
+    a.q = q.data_ptr()
+    a.q_stride[:] = strides(q, 3)
+    a.out = out.data_ptr()
+    a.out_stride[:] = strides(out, 3)
+    a.k_cache = k4.data_ptr()
+    a.k_stride[:] = strides(k4, 4)
+    a.v_cache = v4.data_ptr()
+    a.v_stride[:] = strides(v4, 4)
+    a.block_tables = block_tables.data_ptr()
+    a.block_tables_index = index_code(block_tables)
+    a.block_tables_stride[:] = strides(block_tables, 2)
+    a.seq_lens = seq_lens.data_ptr()
+    a.seq_lens_index = index_code(seq_lens)
+    a.seq_lens_stride = seq_lens.stride(0)
+    if append_k is not None:
+        a.append_k = append_k.data_ptr()
+        a.append_k_stride[:] = strides(append_k, 3)
+        a.append_v = append_v.data_ptr()
+        a.append_v_stride[:] = strides(append_v, 3)
+        a.slot_mapping = slot_mapping.data_ptr()
+        a.slot_mapping_index = index_code(slot_mapping)
+        a.slot_mapping_stride = slot_mapping.stride(0)
+    a.num_splits = int(num_splits)
+    a.epilogue = int(epilogue)
+    if partials is not None:
+        acc, mx, sm = partials
+        a.part_acc = acc.data_ptr()
+        a.part_acc_stride[:] = strides(acc, 4)
+        a.part_max = mx.data_ptr()
+        a.part_sum = sm.data_ptr()
+        a.part_stat_stride[:] = strides(mx, 3)
+    a.max_ctas = int(max_ctas)
+    a.min_tiles_per_cta = int(min_tiles_per_cta)
+    scratch_bytes = ctypes.c_size_t(0)
+    tickets_needed = ctypes.c_int64(0)
+    _lib.check(lib.fd_paged_decode_workspace(ctypes.byref(a), ctypes.byref(scratch_bytes),
+                                             ctypes.byref(tickets_needed)),
+               "fd_paged_decode_workspace")
+    if scratch_bytes.value or tickets_needed.value:
+        tickets, scratch = workspace(q.device, tickets_needed.value, scratch_bytes.value)
+        if tickets is not None:
+            a.tickets = tickets.data_ptr()
+            a.tickets_capacity = tickets.numel()
+        if scratch is not None:
+            a.scratch = scratch.data_ptr()
+            a.scratch_bytes = scratch.numel() * 4
+    _lib.check(lib.fd_paged_decode(ctypes.byref(a), ctypes.c_void_p(stream_handle(q.device))),
+               "fd_paged_decode")
+    return out
+
+
+def split_kv_reduce(acc, mx, sm, seq_lens, out, *, num_seqs, slot_mapping=None):
+    lib = _lib.load_library()
+    a = _lib.SplitReduceArgs()
+    a.struct_size = ctypes.sizeof(_lib.SplitReduceArgs)
+    a.dtype = dtype_code(out)
+    a.num_seqs = int(num_seqs)
+    a.num_q_heads = out.shape[1]
+    a.head_dim = out.shape[2]
+    a.num_splits = acc.shape[2]
+    a.part_acc = acc.data_ptr()
+    a.part_acc_stride[:] = strides(acc, 4)
+    a.part_max = mx.data_ptr()
+    a.part_sum = sm.data_ptr()
+    a.part_stat_stride[:] = strides(mx, 3)
+    a.seq_lens = seq_lens.data_ptr()
+    a.seq_lens_index = index_code(seq_lens)
+    a.seq_lens_stride = seq_lens.stride(0)
+    if slot_mapping is not None:
+        a.slot_mapping = slot_mapping.data_ptr()
+        a.slot_mapping_index = index_code(slot_mapping)
+        a.slot_mapping_stride = slot_mapping.stride(0)
+    a.out = out.data_ptr()
+    a.out_stride[:] = strides(out, 3)
+    _lib.check(lib.fd_split_kv_reduce(ctypes.byref(a), ctypes.c_void_p(stream_handle(out.device))),
+               "fd_split_kv_reduce")
+    return out
+
+
+def rope_kv_append(q, q_out, k, v, k_cache4, v_cache4, block_ids, block_offsets, positions,
+                   rotary_dim, inv_freq):
+    """Launch fd_rope_kv_append; q/q_out may be None (K/V only)."""
+    lib = _lib.load_library()
+    a = _lib.RopeKVAppendArgs()
+    a.struct_size = ctypes.sizeof(_lib.RopeKVAppendArgs)
+    a.dtype = dtype_code(k)
+    a.batch = k.shape[0]
+    a.num_kv_heads = k.shape[1]
+    a.head_dim = k.shape[2]
+    a.rotary_dim = int(rotary_dim)
+    a.block_size = k_cache4.shape[2]
+    a.num_blocks = k_cache4.shape[0]
+    if inv_freq is not None:
+        a.inv_freq = inv_freq.data_ptr()
+    if q is not None:
+        a.num_q_heads = q.shape[1]
+        a.q = q.data_ptr()
+        a.q_stride[:] = strides(q, 3)
+        a.q_out = q_out.data_ptr()
+        a.q_out_stride[:] = strides(q_out, 3)
+    a.k = k.data_ptr()
+    a.k_stride[:] = strides(k, 3)
+    a.v = v.data_ptr()
+    a.v_stride[:] = strides(v, 3)
+    a.k_cache = k_cache4.data_ptr()
+    a.k_cache_stride[:] = strides(k_cache4, 4)
+    a.v_cache = v_cache4.data_ptr()
+    a.v_cache_stride[:] = strides(v_cache4, 4)
+    a.block_ids = block_ids.data_ptr()
+    a.block_offsets = block_offsets.data_ptr()
+    a.block_ids_index = index_code(block_ids)
+    a.block_offsets_index = index_code(block_offsets)
+    if positions is not None:
+        a.positions = positions.data_ptr()
+        a.positions_index = index_code(positions)
+    _lib.check(lib.fd_rope_kv_append(ctypes.byref(a), ctypes.c_void_p(stream_handle(k.device))),
+               "fd_rope_kv_append")
+
+
+# --------------------------------------------------------------------------
+# RoPE frequency tables, computed once per (rotary_dim, base) on the host with
+# the reference formula (flashdec/rope.py:66-67: fp32 arange, fp32 division,
+# fp32 torch.pow) and kept on each device.
+# --------------------------------------------------------------------------
+_freq_lock = threading.Lock()
+_freq_host: dict = {}
+_freq_dev: dict = {}
+
+
+def inv_freq_host(rotary_dim: int, base: float) -> torch.Tensor:
+    key = (int(rotary_dim), float(base))
+    with _freq_lock:
+        t = _freq_host.get(key)
+        if t is None:
+            steps = torch.arange(0, rotary_dim, 2, dtype=torch.float32)
+            t = torch.pow(float(base), -steps / rotary_dim).contiguous()
+            _freq_host[key] = t
+        return t
+
+
+def inv_freq_device(rotary_dim: int, base: float, device) -> torch.Tensor:
+    device = torch.device(device)
+    key = (int(rotary_dim), float(base), device.index)
+    with _freq_lock:
+        t = _freq_dev.get(key)
+    if t is None:
+        host = inv_freq_host(rotary_dim, base)
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("RoPE table not resident on the device; run once before capture")
+        t = host.to(device)
+        with _freq_lock:
+            _freq_dev[key] = t
+    return t

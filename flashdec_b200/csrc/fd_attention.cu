@@ -1,0 +1,1140 @@
+// Paged single-token decode attention for B200 (sm_100a).
+//
+// One kernel covers the reference's three attention kernels
+// (flashdec/kernels/paged_decode.py: per-head MHA :28-121, grouped GQA
+// :124-327, split-KV :330-543) and the fused current-token append of its
+// vLLM launcher (:728-919).  A standalone reducer covers :546-642.
+//
+// Work decomposition.  The unit of work is a 32-token tile of one
+// (sequence, head block) pair; a head block is up to 16 query heads that share
+// one KV head, so every K/V byte is read once per head block (once per KV head
+// whenever the GQA group is <= 16).  Two schedules:
+//   * num_splits == 0 (auto): the tiles of the whole batch are laid out in
+//     (sequence, head block, tile) order and cut into equal ranges, one per
+//     persistent CTA.  A CTA's range may cover the tail of one pair, whole
+//     pairs and the head of another; every piece is a "segment".  This
+//     balances ragged batches to within one tile per SM.
+//   * num_splits == S: the reference's fixed split of every sequence into S
+//     chunks of cdiv(tiles, S) tiles (paged_decode.py:395-411), one CTA each.
+// A segment that covers a whole pair writes the output directly.  Otherwise
+// it writes an un-normalised partial (acc, max, sum) and takes a ticket; the
+// CTA that takes the last ticket of the pair merges all partials (the reducer
+// runs inside the kernel: no second launch and no CTA ever waits for another)
+// and re-arms the ticket for the next call.
+//
+// Inside a CTA: warp 4 is the producer.  It resolves block-table entries
+// (32 at a time, one per lane) and issues one TMA box per (page, 64-dim half)
+// into a ring of shared-memory stages (128B swizzle; one "full" and one
+// "empty" mbarrier per stage).  Caches whose strides a tensor map cannot
+// describe are copied by the producer warp with ordinary loads instead.
+// Warps 0-3 are consumers: each takes whole tiles round robin and runs
+// S = Q K^T and O += P V on the tensor cores (mma.sync m16n8k16, fp32
+// accumulate) with an online softmax in fp32 (base-2 exponent, scale folded
+// in).  At the end of a segment the four warps' (m, l, O) are merged through
+// shared memory.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "fd_host.h"
+#include "fd_ptx.cuh"
+
+namespace fd {
+
+constexpr int kTile = 32;  // tokens per tile
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumerThreads = 32 * kConsumerWarps;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kMaxRows = 16;  // query heads per head block (mma M)
+constexpr int kMaxStages = 16;
+constexpr int kMiscInts = 8;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kBarConsumers = 1;  // named barrier id for the consumer warps
+
+struct AttnParams {
+  int num_seqs, num_q_heads, num_kv_heads, block_size, num_blocks, max_blocks;
+  int group, hb_per_kv, rows, nhb;
+  float scale_log2;  // sm_scale * log2(e)
+  const void* q;
+  int64_t qs0, qs1, qs2;
+  void* out;
+  int64_t os0, os1, os2;
+  void* k;
+  int64_t ks0, ks1, ks2, ks3;
+  void* v;
+  int64_t vs0, vs1, vs2, vs3;
+  int kperm[3], vperm[3];  // tensor-map axis order (0 token, 1 head, 2 block)
+  const void* bt;
+  int bt64;
+  int64_t bts0, bts1;
+  const void* sl;
+  int sl64;
+  int64_t sls;
+  const void* ak;
+  int64_t aks0, aks1, aks2;
+  const void* av;
+  int64_t avs0, avs1, avs2;
+  const void* slot;
+  int slot64;
+  int64_t slots;
+  int fused_append;
+  int num_splits;  // 0 = length-balanced (stream-K) schedule
+  int epilogue;    // FD_EPILOGUE_*
+  int min_tiles_per_cta;
+  // split-mode partials [seq, q_head, split, dim] / [seq, q_head, split]
+  float* pacc;
+  int64_t pas0, pas1, pas2, pas3;
+  float* pmax;
+  float* psum;
+  int64_t pss0, pss1, pss2;
+  // stream-K partial slots: acc[(slot*rows + r)*D + d], m/l[slot*rows + r]
+  float* slot_acc;
+  float* slot_m;
+  float* slot_l;
+  int* tickets;
+  int* status;
+  int num_stages;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kHalfBytes = kTile * 128;  // [32 rows][64 dims] x 2 B
+  static constexpr int kStageBytes = 2 * kHalves * kHalfBytes;
+  static constexpr int kMergeFloats = kConsumerWarps * kMaxRows * D;
+  static constexpr int kMergeBytes = kMergeFloats * 4 + kConsumerWarps * kMaxRows * 8;
+};
+
+// Byte offset of element (row, dim) in a [32][D] tile stored as D/64 halves
+// of [32][64] with the TMA 128B swizzle (16-byte chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t tile_offset(int row, int dim) {
+  const int dd = dim & 63;
+  return (dim >> 6) * (kTile * 128) + row * 128 + (((dd >> 3) ^ (row & 7)) << 4) + ((dd & 7) << 1);
+}
+
+// Byte offset of 16-byte chunk `chunk` (8 dims) of `row`.
+__device__ __forceinline__ uint32_t chunk_offset(int row, int chunk) {
+  return (chunk >> 3) * (kTile * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+}
+
+struct SeqInfo {
+  int n;      // tokens attended (0 => nothing to attend: zero output)
+  int tiles;  // cdiv(n, 32)
+};
+
+// Reference semantics (paged_decode.py:263-264, :398-403): the sequence is
+// active when seq_len > 0 and, with a fused append, slot >= 0.  seq_len is
+// clamped to the block-table capacity so no read leaves the table row.
+__device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
+  int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
+  const int64_t cap = static_cast<int64_t>(p.max_blocks) * p.block_size;
+  n = n < 0 ? 0 : (n > cap ? cap : n);
+  if (p.fused_append && n > 0) {
+    const int64_t s = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
+    if (s < 0) n = 0;
+  }
+  SeqInfo r;
+  r.n = static_cast<int>(n);
+  r.tiles = static_cast<int>((n + kTile - 1) / kTile);
+  return r;
+}
+
+// A piece of work: tiles [t0, t1) of pair (b, hb).
+struct Segment {
+  int b, hb, t0, t1, n, tiles;
+  int whole;      // covers the whole pair: write the output directly
+  int part_slot;  // stream-K slot id or split index
+  int nseg;       // contributors to the pair's ticket
+  int c_first;    // stream-K: first contributing CTA
+};
+
+struct Sched {
+  const int* prefix;  // smem, tiles prefix over sequences [num_seqs + 1]
+  int64_t U;          // total tiles of the batch
+  int g;              // CTAs that own work (<= gridDim.x)
+  int64_t x, hi;      // this CTA's cursor / end (stream-K)
+  int done;           // split mode: the single segment was produced
+  __device__ __forceinline__ int64_t lo(int c) const { return (static_cast<int64_t>(c) * U) / g; }
+  // CTA owning linear tile x (largest c with lo(c) <= x)
+  __device__ __forceinline__ int owner(int64_t x_) const {
+    return static_cast<int>(((x_ + 1) * g + U - 1) / U) - 1;
+  }
+};
+
+__device__ __forceinline__ int find_seq(const int* prefix, int num_seqs, int nhb, int64_t x) {
+  // largest b with nhb * prefix[b] <= x; empty sequences before a non-empty
+  // one share its start, and the search lands on the last of them, i.e. the
+  // non-empty one that actually contains x.
+  int lo = 0, hi = num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (static_cast<int64_t>(nhb) * prefix[mid] <= x) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Segment& s) {
+  if (p.num_splits == 0) {
+    if (sc.x >= sc.hi) return false;
+    const int b = find_seq(sc.prefix, p.num_seqs, p.nhb, sc.x);
+    const int tiles = sc.prefix[b + 1] - sc.prefix[b];
+    const int64_t seq_base = static_cast<int64_t>(p.nhb) * sc.prefix[b];
+    const int hb = static_cast<int>((sc.x - seq_base) / tiles);
+    const int64_t pair_start = seq_base + static_cast<int64_t>(hb) * tiles;
+    const int64_t pair_end = pair_start + tiles;
+    const int64_t seg_end = pair_end < sc.hi ? pair_end : sc.hi;
+    s.b = b;
+    s.hb = hb;
+    s.tiles = tiles;
+    s.t0 = static_cast<int>(sc.x - pair_start);
+    s.t1 = static_cast<int>(seg_end - pair_start);
+    s.whole = (s.t0 == 0 && s.t1 == tiles);
+    s.c_first = sc.owner(pair_start);
+    s.nseg = sc.owner(pair_end - 1) - s.c_first + 1;
+    s.part_slot = static_cast<int>(blockIdx.x) + b * p.nhb + hb;
+    s.n = seq_info(p, b).n;
+    sc.x = seg_end;
+    return true;
+  }
+  if (sc.done) return false;
+  sc.done = 1;
+  const int S = p.num_splits;
+  const int pid = static_cast<int>(blockIdx.x) / S;
+  const int split = static_cast<int>(blockIdx.x) % S;
+  if (pid >= p.num_seqs * p.nhb) return false;
+  s.b = pid / p.nhb;
+  s.hb = pid % p.nhb;
+  const SeqInfo si = seq_info(p, s.b);
+  s.n = si.n;
+  s.tiles = si.tiles;
+  const int bps = (si.tiles + S - 1) / S;
+  const int t0 = min(split * bps, si.tiles);
+  const int t1 = min(t0 + bps, si.tiles);
+  s.t0 = t0;
+  s.t1 = t1 > t0 ? t1 : t0;
+  s.whole = (S == 1) && p.epilogue == FD_EPILOGUE_FUSED;
+  s.part_slot = split;
+  s.nseg = S;
+  s.c_first = 0;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// partial storage
+// ---------------------------------------------------------------------------
+template <int D>
+struct PartRef {
+  float* acc;  // points at element d = 0 of (slot, row)
+  int64_t acc_step_d;
+  float* m;
+  float* l;
+};
+
+template <int D>
+__device__ __forceinline__ PartRef<D> part_ref(const AttnParams& p, const Segment& s, int slot,
+                                               int row, int qhead) {
+  PartRef<D> r;
+  if (p.num_splits == 0) {
+    const int64_t i = static_cast<int64_t>(slot) * p.rows + row;
+    r.acc = p.slot_acc + i * D;
+    r.acc_step_d = 1;
+    r.m = p.slot_m + i;
+    r.l = p.slot_l + i;
+  } else {
+    r.acc = p.pacc + s.b * p.pas0 + qhead * p.pas1 + slot * p.pas2;
+    r.acc_step_d = p.pas3;
+    const int64_t o = s.b * p.pss0 + qhead * p.pss1 + slot * p.pss2;
+    r.m = p.pmax + o;
+    r.l = p.psum + o;
+  }
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_out4(const AttnParams& p, int b, int h, int d, float a0,
+                                           float a1, float a2, float a3) {
+  T* o = static_cast<T*>(p.out) + b * p.os0 + h * p.os1 + d * p.os2;
+  o[0] = from_f32<T>(a0);
+  o[p.os2] = from_f32<T>(a1);
+  o[2 * p.os2] = from_f32<T>(a2);
+  o[3 * p.os2] = from_f32<T>(a3);
+}
+
+__device__ __forceinline__ int tmap_coord(int axis, int kv_head, int blk) {
+  return axis == 0 ? 0 : (axis == 1 ? kv_head : blk);
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <typename T, int D, bool kTma>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_decode_kernel(const __grid_constant__ AttnParams p,
+                        const __grid_constant__ CUtensorMap tmap_k,
+                        const __grid_constant__ CUtensorMap tmap_v) {
+  using SM = Smem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int NST = p.num_stages;
+  uint8_t* stages = smem;
+  float* obuf = reinterpret_cast<float*>(stages + NST * SM::kStageBytes);
+  float2* mlbuf = reinterpret_cast<float2*>(obuf + SM::kMergeFloats);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(mlbuf + kConsumerWarps * kMaxRows);
+  uint64_t* empty_bar = full_bar + NST;
+  uint32_t* stage_mask = reinterpret_cast<uint32_t*>(empty_bar + NST);
+  int* misc = reinterpret_cast<int*>(stage_mask + NST);  // [0] abort, [1] ticket winner
+  int* prefix = misc + kMiscInts;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  volatile int* abort_flag = misc;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    misc[0] = 0;
+    misc[1] = 0;
+    fence_mbar_init();
+  }
+  if (kTma && warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+
+  // ---- schedule ----------------------------------------------------------
+  Sched sc;
+  sc.prefix = prefix;
+  sc.U = 0;
+  sc.g = 1;
+  sc.x = sc.hi = 0;
+  sc.done = 0;
+  const bool streamk = (p.num_splits == 0);
+  if (streamk) {
+    for (int b = tid; b < p.num_seqs; b += kThreads) prefix[b + 1] = seq_info(p, b).tiles;
+    if (tid == 0) prefix[0] = 0;
+  }
+  __syncthreads();
+  if (streamk) {
+    if (warp == 0) {  // chunked inclusive scan of prefix[1..num_seqs]
+      const int n = p.num_seqs;
+      const int per = (n + 31) / 32;
+      const int beg = 1 + lane * per;
+      const int end = min(beg + per, n + 1);
+      int run = 0;
+      for (int i = beg; i < end; ++i) {
+        run += prefix[i];
+        prefix[i] = run;
+      }
+      int incl = run;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = incl - run;
+      for (int i = beg; i < end; ++i) prefix[i] += excl;
+    }
+    __syncthreads();
+    sc.U = static_cast<int64_t>(p.nhb) * prefix[p.num_seqs];
+    int64_t g = (sc.U + p.min_tiles_per_cta - 1) / p.min_tiles_per_cta;
+    if (g > static_cast<int64_t>(gridDim.x)) g = gridDim.x;
+    sc.g = static_cast<int>(g < 1 ? 1 : g);
+    if (sc.U > 0 && static_cast<int>(blockIdx.x) < sc.g) {
+      sc.x = sc.lo(blockIdx.x);
+      sc.hi = sc.lo(blockIdx.x + 1);
+    }
+  }
+
+  const int bs = p.block_size;
+  const int PPT = kTile / bs;  // pages per tile: 1, 2 or 4
+
+  // =========================================================================
+  // producer warp
+  // =========================================================================
+  if (warp == kConsumerWarps) {
+    const uint64_t policy = l2_policy_evict_first();
+    uint32_t iter = 0;
+    Segment s;
+    while (next_segment(p, sc, s)) {
+      if (s.t1 <= s.t0) continue;
+      const int kv_head = s.hb / p.hb_per_kv;
+      const int limit_cache = p.fused_append ? s.n - 1 : s.n;  // tokens read from the cache
+      const int nlb = (limit_cache + bs - 1) / bs;              // pages holding them
+      const int64_t lb_begin = static_cast<int64_t>(s.t0) * PPT;
+      const int64_t lb_end = min(static_cast<int64_t>(s.t1) * PPT, static_cast<int64_t>(nlb));
+      const char* bt_row = static_cast<const char*>(p.bt);
+      auto load_entry = [&](int64_t lb) -> int {
+        if (lb >= lb_end) return -1;
+        return static_cast<int>(
+            load_index(p.bt, p.bt64, static_cast<int64_t>(s.b) * p.bts0 + lb * p.bts1));
+      };
+      (void)bt_row;
+      int64_t chunk_base = lb_begin;
+      int cur = load_entry(chunk_base + lane);
+      int nxt = load_entry(chunk_base + 32 + lane);
+      bool bad = false;
+      for (int t = s.t0; t < s.t1; ++t, ++iter) {
+        const int stage = static_cast<int>(iter % NST);
+        const uint32_t phase = (iter / NST) & 1u;
+        const bool ok = mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.status, abort_flag);
+        uint32_t mask = 0;
+        int blk_of[4] = {-1, -1, -1, -1};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (j < PPT) {
+            const int64_t lb = static_cast<int64_t>(t) * PPT + j;
+            while (lb >= chunk_base + 32) {  // warp-uniform
+              chunk_base += 32;
+              cur = nxt;
+              nxt = load_entry(chunk_base + 32 + lane);
+            }
+            const int blk = __shfl_sync(0xffffffffu, cur, static_cast<int>(lb - chunk_base));
+            if (lb < lb_end) {
+              if (blk >= 0 && blk < p.num_blocks) {
+                mask |= 1u << j;
+                blk_of[j] = blk;
+              } else {
+                bad = true;
+              }
+            }
+          }
+        }
+        if (!ok) continue;
+        const uint32_t sbase = smem_u32(stages + stage * SM::kStageBytes);
+        if constexpr (kTma) {
+          if (lane == 0) {
+            stage_mask[stage] = mask;
+            const uint32_t bytes = __popc(mask) * bs * D * 2 * 2;
+            const uint32_t fb = smem_u32(&full_bar[stage]);
+            mbar_arrive_expect_tx(fb, bytes);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (mask & (1u << j)) {
+                const int blk = blk_of[j];
+#pragma unroll
+                for (int h = 0; h < SM::kHalves; ++h) {
+                  const uint32_t off = h * SM::kHalfBytes + j * bs * 128;
+                  tma_load_4d(sbase + off, &tmap_k, fb, h * 64,
+                              tmap_coord(p.kperm[0], kv_head, blk),
+                              tmap_coord(p.kperm[1], kv_head, blk),
+                              tmap_coord(p.kperm[2], kv_head, blk), policy);
+                  tma_load_4d(sbase + SM::kHalves * SM::kHalfBytes + off, &tmap_v, fb, h * 64,
+                              tmap_coord(p.vperm[0], kv_head, blk),
+                              tmap_coord(p.vperm[1], kv_head, blk),
+                              tmap_coord(p.vperm[2], kv_head, blk), policy);
+                }
+              }
+            }
+          }
+        } else {
+          // generic strides: the producer warp copies the valid pages itself
+          uint8_t* sb = stages + stage * SM::kStageBytes;
+          for (int j = 0; j < PPT; ++j) {
+            if (!(mask & (1u << j))) continue;
+            const int blk = blk_of[j];
+            const uint16_t* kp = static_cast<const uint16_t*>(p.k) + blk * p.ks0 + kv_head * p.ks1;
+            const uint16_t* vp = static_cast<const uint16_t*>(p.v) + blk * p.vs0 + kv_head * p.vs1;
+            for (int e = lane; e < bs * D; e += 32) {
+              const int r = e / D;
+              const int d = e - r * D;
+              const uint32_t off = tile_offset(j * bs + r, d);
+              *reinterpret_cast<uint16_t*>(sb + off) = kp[r * p.ks2 + d * p.ks3];
+              *reinterpret_cast<uint16_t*>(sb + SM::kHalves * SM::kHalfBytes + off) =
+                  vp[r * p.vs2 + d * p.vs3];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
+            stage_mask[stage] = mask;
+            mbar_arrive(smem_u32(&full_bar[stage]));
+          }
+        }
+      }
+      if (bad && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+    }
+    return;
+  }
+
+  // =========================================================================
+  // consumer warps
+  // =========================================================================
+  const int g8 = lane >> 2;  // mma group (row) index
+  const int t4 = lane & 3;   // thread in group
+  const int mi = lane >> 3;  // ldmatrix matrix index
+  const int r8 = lane & 7;   // ldmatrix row
+  uint32_t iter = 0;
+  Segment s;
+  while (next_segment(p, sc, s)) {
+    const int kv_head = s.hb / p.hb_per_kv;
+    const int jblk = s.hb % p.hb_per_kv;
+    const int head0 = kv_head * p.group + jblk * p.rows;
+    const int nrows = min(p.rows, p.group - jblk * p.rows);
+
+    // ---- Q fragments (A operand, rows = query heads) ----
+    uint32_t qf[D / 16][4];
+    {
+      const T* qb = static_cast<const T*>(p.q) + s.b * p.qs0;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int row = g8 + ((rr & 1) ? 8 : 0);
+          const int d = ks * 16 + 2 * t4 + ((rr & 2) ? 8 : 0);
+          float a = 0.f, c = 0.f;
+          if (row < nrows) {
+            const T* qr = qb + (head0 + row) * p.qs1;
+            a = to_f32<T>(qr[d * p.qs2]);
+            c = to_f32<T>(qr[(d + 1) * p.qs2]);
+          }
+          qf[ks][rr] = pack2<T>(a, c);
+        }
+      }
+    }
+
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+
+    const int limit_cache = p.fused_append ? s.n - 1 : s.n;
+    for (int t = s.t0; t < s.t1; ++t, ++iter) {
+      if (static_cast<int>(iter % kConsumerWarps) != warp) continue;
+      const int stage = static_cast<int>(iter % NST);
+      const uint32_t phase = (iter / NST) & 1u;
+      if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, abort_flag)) continue;
+      uint8_t* sb = stages + stage * SM::kStageBytes;
+      const uint32_t kbase = smem_u32(sb);
+      const uint32_t vbase = kbase + SM::kHalves * SM::kHalfBytes;
+      const uint32_t pmask = stage_mask[stage];
+      const int base = t * kTile;
+
+      // valid rows of this tile
+      const int pos = base + lane;
+      const bool from_cache = pos < limit_cache && ((pmask >> (lane / bs)) & 1u);
+      const bool appended = p.fused_append && pos == s.n - 1;
+      const uint32_t vmask = __ballot_sync(0xffffffffu, from_cache || appended);
+      bool touched = false;
+      if (vmask != 0xffffffffu) {
+        // rows without data: zero V so that P (= 0 there) times V stays 0
+        // even if the stale bytes are NaN/Inf.
+        const uint32_t inv = ~vmask;
+        for (int e = lane; e < kTile * (D / 8); e += 32) {
+          const int r = e / (D / 8);
+          const int c = e - r * (D / 8);
+          if ((inv >> r) & 1u) {
+            *reinterpret_cast<uint4*>(sb + SM::kHalves * SM::kHalfBytes + chunk_offset(r, c)) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        touched = true;
+      }
+      if (p.fused_append && (s.n - 1) >= base && (s.n - 1) < base + kTile) {
+        // current token: K/V come from the call; patch the tile and store the
+        // token into its cache slot (reference paged_decode.py:193-221).
+        const int ra = s.n - 1 - base;
+        const T* akp = static_cast<const T*>(p.ak) + s.b * p.aks0 + kv_head * p.aks1;
+        const T* avp = static_cast<const T*>(p.av) + s.b * p.avs0 + kv_head * p.avs1;
+        const int64_t slot = load_index(p.slot, p.slot64, static_cast<int64_t>(s.b) * p.slots);
+        const int64_t sblk = slot / bs;
+        const int64_t soff = slot - sblk * bs;
+        const bool store = (jblk == 0) && sblk < p.num_blocks;
+        T* kc = static_cast<T*>(p.k) + sblk * p.ks0 + kv_head * p.ks1 + soff * p.ks2;
+        T* vc = static_cast<T*>(p.v) + sblk * p.vs0 + kv_head * p.vs1 + soff * p.vs2;
+        for (int d = lane; d < D; d += 32) {
+          const T kv = akp[d * p.aks2];
+          const T vv = avp[d * p.avs2];
+          *reinterpret_cast<T*>(sb + tile_offset(ra, d)) = kv;
+          *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes + tile_offset(ra, d)) = vv;
+          if (store) {
+            kc[d * p.ks3] = kv;
+            vc[d * p.vs3] = vv;
+          }
+        }
+        if (!store && jblk == 0 && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+        touched = true;
+      }
+      if (touched) __syncwarp();
+
+      // ---- S = Q K^T  (16 heads x 32 tokens) ----
+      float sacc[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          const int tok = np * 16 + (mi >> 1) * 8 + r8;
+          const int chunk = ks * 2 + (mi & 1);
+          uint32_t b0a, b1a, b0b, b1b;
+          ldsm_x4(kbase + chunk_offset(tok, chunk), b0a, b1a, b0b, b1b);
+          mma_16816<T>(sacc[2 * np], qf[ks], b0a, b1a);
+          mma_16816<T>(sacc[2 * np + 1], qf[ks], b0b, b1b);
+        }
+      }
+
+      // ---- online softmax (base 2, scale folded in) ----
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tok = 8 * j + 2 * t4 + e;
+          const bool valid = (vmask >> tok) & 1u;
+          const float x0 = valid ? sacc[j][e] * p.scale_log2 : -INFINITY;
+          const float x1 = valid ? sacc[j][2 + e] * p.scale_log2 : -INFINITY;
+          sacc[j][e] = x0;
+          sacc[j][2 + e] = x1;
+          mx0 = fmaxf(mx0, x0);
+          mx1 = fmaxf(mx1, x1);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0);
+      const float mn1 = fmaxf(m1, mx1);
+      const float ref0 = (mn0 == -INFINITY) ? 0.f : mn0;
+      const float ref1 = (mn1 == -INFINITY) ? 0.f : mn1;
+      const float alpha0 = exp2f(m0 - ref0);
+      const float alpha1 = exp2f(m1 - ref1);
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sacc[j][0] = exp2f(sacc[j][0] - ref0);
+        sacc[j][1] = exp2f(sacc[j][1] - ref0);
+        sacc[j][2] = exp2f(sacc[j][2] - ref1);
+        sacc[j][3] = exp2f(sacc[j][3] - ref1);
+        ps0 += sacc[j][0] + sacc[j][1];
+        ps1 += sacc[j][2] + sacc[j][3];
+      }
+      l0 = l0 * alpha0 + ps0;
+      l1 = l1 * alpha1 + ps1;
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) {
+        o[j][0] *= alpha0;
+        o[j][1] *= alpha0;
+        o[j][2] *= alpha1;
+        o[j][3] *= alpha1;
+      }
+
+      // ---- O += P V ----
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        uint32_t a[4];
+        a[0] = pack2<T>(sacc[2 * kk][0], sacc[2 * kk][1]);
+        a[1] = pack2<T>(sacc[2 * kk][2], sacc[2 * kk][3]);
+        a[2] = pack2<T>(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+        a[3] = pack2<T>(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+#pragma unroll
+        for (int dp = 0; dp < D / 16; ++dp) {
+          const int tok = kk * 16 + (mi & 1) * 8 + r8;
+          const int chunk = dp * 2 + (mi >> 1);
+          uint32_t b0a, b1a, b0b, b1b;
+          ldsm_x4_t(vbase + chunk_offset(tok, chunk), b0a, b1a, b0b, b1b);
+          mma_16816<T>(o[2 * dp], a, b0a, b1a);
+          mma_16816<T>(o[2 * dp + 1], a, b0b, b1b);
+        }
+      }
+      __syncwarp();
+      if (touched) fence_proxy_async_smem();
+      if (lane == 0) mbar_arrive(smem_u32(&empty_bar[stage]));
+    }
+
+    // ---- merge the four warps' states of this segment ----
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if (t4 == 0) {
+      mlbuf[warp * kMaxRows + g8] = make_float2(m0, l0);
+      mlbuf[warp * kMaxRows + g8 + 8] = make_float2(m1, l1);
+    }
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      const int d = 8 * j + 2 * t4;
+      *reinterpret_cast<float2*>(&obuf[(warp * kMaxRows + g8) * D + d]) =
+          make_float2(o[j][0], o[j][1]);
+      *reinterpret_cast<float2*>(&obuf[(warp * kMaxRows + g8 + 8) * D + d]) =
+          make_float2(o[j][2], o[j][3]);
+    }
+    named_barrier(kBarConsumers, kConsumerThreads);
+    const int pid = s.b * p.nhb + s.hb;
+    for (int e = tid; e < nrows * (D / 4); e += kConsumerThreads) {
+      const int r = e / (D / 4);
+      const int d = (e - r * (D / 4)) * 4;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlbuf[w * kMaxRows + r].x);
+      float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float2 ml = mlbuf[w * kMaxRows + r];
+          const float wgt = exp2f(ml.x - M);
+          const float4 ov = *reinterpret_cast<const float4*>(&obuf[(w * kMaxRows + r) * D + d]);
+          L += wgt * ml.y;
+          a0 += wgt * ov.x;
+          a1 += wgt * ov.y;
+          a2 += wgt * ov.z;
+          a3 += wgt * ov.w;
+        }
+      }
+      if (s.whole) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        store_out4<T>(p, s.b, head0 + r, d, a0 * inv, a1 * inv, a2 * inv, a3 * inv);
+      } else {
+        PartRef<D> pr = part_ref<D>(p, s, s.part_slot, r, head0 + r);
+        float* ap = pr.acc + d * pr.acc_step_d;
+        ap[0] = a0;
+        ap[pr.acc_step_d] = a1;
+        ap[2 * pr.acc_step_d] = a2;
+        ap[3 * pr.acc_step_d] = a3;
+        if (d == 0) {
+          *pr.m = (M == -INFINITY) ? -INFINITY : M * kLn2;  // natural-log units
+          *pr.l = L;
+        }
+      }
+    }
+    if (!s.whole && p.epilogue == FD_EPILOGUE_FUSED) {
+      __threadfence();
+      named_barrier(kBarConsumers, kConsumerThreads);
+      if (tid == 0) {
+        const int prev = atomicAdd(&p.tickets[pid], 1);
+        const int last = (prev == s.nseg - 1);
+        if (last) atomicExch(&p.tickets[pid], 0);  // re-arm for the next call
+        misc[1] = last;
+      }
+      named_barrier(kBarConsumers, kConsumerThreads);
+      if (misc[1]) {
+        __threadfence();
+        // final merge of the pair's nseg partials (reference reducer
+        // semantics, paged_decode.py:593-635)
+        for (int e = tid; e < nrows * (D / 4); e += kConsumerThreads) {
+          const int r = e / (D / 4);
+          const int d = (e - r * (D / 4)) * 4;
+          float M = -INFINITY;
+          for (int i = 0; i < s.nseg; ++i) {
+            const int sl = (p.num_splits == 0) ? (s.c_first + i + pid) : i;
+            M = fmaxf(M, __ldcg(part_ref<D>(p, s, sl, r, head0 + r).m));
+          }
+          float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+          if (M != -INFINITY) {
+            for (int i = 0; i < s.nseg; ++i) {
+              const int sl = (p.num_splits == 0) ? (s.c_first + i + pid) : i;
+              PartRef<D> pr = part_ref<D>(p, s, sl, r, head0 + r);
+              const float mi_ = __ldcg(pr.m);
+              if (mi_ == -INFINITY) continue;
+              const float wgt = exp2f((mi_ - M) * kLog2e);
+              L += wgt * __ldcg(pr.l);
+              const float* ap = pr.acc + d * pr.acc_step_d;
+              a0 += wgt * __ldcg(ap);
+              a1 += wgt * __ldcg(ap + pr.acc_step_d);
+              a2 += wgt * __ldcg(ap + 2 * pr.acc_step_d);
+              a3 += wgt * __ldcg(ap + 3 * pr.acc_step_d);
+            }
+          }
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+          store_out4<T>(p, s.b, head0 + r, d, a0 * inv, a1 * inv, a2 * inv, a3 * inv);
+        }
+      }
+    }
+    named_barrier(kBarConsumers, kConsumerThreads);
+  }
+
+  // ---- zero outputs of pairs with nothing to attend (stream-K) ----
+  if (streamk) {
+    for (int b = 0; b < p.num_seqs; ++b) {
+      if (prefix[b + 1] != prefix[b]) continue;
+      for (int hb = 0; hb < p.nhb; ++hb) {
+        if ((b * p.nhb + hb) % static_cast<int>(gridDim.x) != static_cast<int>(blockIdx.x)) continue;
+        const int kvh = hb / p.hb_per_kv;
+        const int jb = hb % p.hb_per_kv;
+        const int h0 = kvh * p.group + jb * p.rows;
+        const int nr = min(p.rows, p.group - jb * p.rows);
+        for (int e = tid; e < nr * (D / 4); e += kConsumerThreads) {
+          const int r = e / (D / 4);
+          store_out4<T>(p, b, h0 + r, (e - r * (D / 4)) * 4, 0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// standalone split-KV reducer (reference _paged_decode_gqa_reduce_kernel)
+// ---------------------------------------------------------------------------
+struct ReduceParams {
+  int num_seqs, num_q_heads, head_dim, num_splits;
+  const float* acc;
+  int64_t as0, as1, as2, as3;
+  const float* mx;
+  const float* sm;
+  int64_t ss0, ss1, ss2;
+  const void* sl;
+  int sl64;
+  int64_t sls;
+  const void* slot;
+  int slot64;
+  int64_t slots;
+  void* out;
+  int64_t os0, os1, os2;
+};
+
+template <typename T>
+__global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
+  const int b = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
+  bool has = n > 0;
+  if (p.slot) has = has && load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) >= 0;
+  float M = -INFINITY;
+  if (has) {
+    for (int s = 0; s < p.num_splits; ++s) {
+      M = fmaxf(M, p.mx[b * p.ss0 + h * p.ss1 + s * p.ss2]);
+    }
+  }
+  for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
+    float L = 0.f, a = 0.f;
+    if (has && M != -INFINITY) {
+      for (int s = 0; s < p.num_splits; ++s) {
+        const int64_t so = b * p.ss0 + h * p.ss1 + s * p.ss2;
+        const float m = p.mx[so];
+        if (m == -INFINITY) continue;
+        const float w = exp2f((m - M) * kLog2e);
+        L += w * p.sm[so];
+        a += w * p.acc[b * p.as0 + h * p.as1 + s * p.as2 + d * p.as3];
+      }
+    }
+    T* o = static_cast<T*>(p.out) + b * p.os0 + h * p.os1 + d * p.os2;
+    *o = from_f32<T>(L > 0.f ? a / L : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+template <int D>
+size_t smem_bytes(int stages, int sched_ints) {
+  using SM = Smem<D>;
+  return 1024 + static_cast<size_t>(stages) * SM::kStageBytes + SM::kMergeBytes +
+         static_cast<size_t>(stages) * 20 + (kMiscInts + sched_ints) * sizeof(int);
+}
+
+struct Derived {
+  int group, hb_per_kv, rows, nhb;
+};
+
+Derived derive(const fd_paged_decode_args& a) {
+  Derived d;
+  d.group = a.num_q_heads / a.num_kv_heads;
+  d.hb_per_kv = (d.group + kMaxRows - 1) / kMaxRows;
+  d.rows = (d.group + d.hb_per_kv - 1) / d.hb_per_kv;
+  d.nhb = a.num_kv_heads * d.hb_per_kv;
+  return d;
+}
+
+int validate(const fd_paged_decode_args* a) {
+  if (!a || a->struct_size != static_cast<int32_t>(sizeof(fd_paged_decode_args)))
+    return FD_ERR_INVALID_ARGUMENT;
+  if (a->dtype != FD_DTYPE_F16 && a->dtype != FD_DTYPE_BF16) return FD_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128) return FD_ERR_UNSUPPORTED;
+  if (a->block_size != 8 && a->block_size != 16 && a->block_size != 32) return FD_ERR_UNSUPPORTED;
+  if (a->num_seqs < 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->num_blocks <= 0 ||
+      a->max_blocks_per_seq <= 0)
+    return FD_ERR_INVALID_ARGUMENT;
+  if (a->num_q_heads % a->num_kv_heads != 0) return FD_ERR_INVALID_ARGUMENT;
+  if (!a->q || !a->out || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens)
+    return FD_ERR_INVALID_ARGUMENT;
+  if (a->append_k && (!a->append_v || !a->slot_mapping)) return FD_ERR_INVALID_ARGUMENT;
+  if (a->num_splits < 0 || a->num_splits > 4096) return FD_ERR_INVALID_ARGUMENT;
+  if (a->epilogue != FD_EPILOGUE_FUSED && a->epilogue != FD_EPILOGUE_PARTIALS)
+    return FD_ERR_INVALID_ARGUMENT;
+  if (a->epilogue == FD_EPILOGUE_PARTIALS && a->num_splits == 0) return FD_ERR_INVALID_ARGUMENT;
+  return FD_OK;
+}
+
+int grid_for(const fd_paged_decode_args& a, const Derived& dv, const DeviceInfo& dev) {
+  if (a.num_splits == 0) {
+    int g = a.max_ctas > 0 ? a.max_ctas : dev.num_sms;
+    return g < 1 ? 1 : g;
+  }
+  return a.num_seqs * dv.nhb * a.num_splits;
+}
+
+struct WorkspaceNeed {
+  size_t scratch_bytes = 0;
+  int64_t tickets = 0;
+};
+
+WorkspaceNeed workspace_need(const fd_paged_decode_args& a, const Derived& dv, int grid) {
+  WorkspaceNeed w;
+  const int64_t pairs = static_cast<int64_t>(a.num_seqs) * dv.nhb;
+  if (a.num_splits == 0) {
+    const int64_t slots = static_cast<int64_t>(grid) + pairs;
+    w.scratch_bytes = static_cast<size_t>(slots) * dv.rows * (a.head_dim + 2) * sizeof(float);
+    w.tickets = pairs;
+  } else {
+    const bool partials = a.num_splits > 1 || a.epilogue == FD_EPILOGUE_PARTIALS;
+    if (partials && !a.part_acc) {
+      w.scratch_bytes = static_cast<size_t>(a.num_seqs) * a.num_q_heads * a.num_splits *
+                        (a.head_dim + 2) * sizeof(float);
+    }
+    if (a.num_splits > 1 && a.epilogue == FD_EPILOGUE_FUSED) w.tickets = pairs;
+  }
+  return w;
+}
+
+template <typename T, int D, bool kTma>
+int launch(const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv, int grid,
+           size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
+  auto kern = paged_decode_kernel<T, D, kTma>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  const int slot = dev.device & 63;
+  std::call_once(once[slot], [&] {
+    attr_err[slot] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          dev.max_smem_optin);
+  });
+  if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
+  kern<<<grid, kThreads, smem, stream>>>(prm, mk, mv);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename T, int D>
+int dispatch_tma(bool tma, const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
+                 int grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
+  return tma ? launch<T, D, true>(prm, mk, mv, grid, smem, dev, st)
+             : launch<T, D, false>(prm, mk, mv, grid, smem, dev, st);
+}
+
+}  // namespace
+}  // namespace fd
+
+using namespace fd;
+
+extern "C" int fd_paged_decode_workspace(const fd_paged_decode_args* a, size_t* scratch_bytes,
+                                         int64_t* tickets_needed) {
+  int rc = validate(a);
+  if (rc) return rc;
+  const DeviceInfo* dev = current_device_info();
+  if (!dev) return FD_ERR_CUDA;
+  const Derived dv = derive(*a);
+  const WorkspaceNeed w = workspace_need(*a, dv, grid_for(*a, dv, *dev));
+  if (scratch_bytes) *scratch_bytes = w.scratch_bytes;
+  if (tickets_needed) *tickets_needed = w.tickets;
+  return FD_OK;
+}
+
+extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream) {
+  int rc = validate(a);
+  if (rc) return rc;
+  if (a->num_seqs == 0) return FD_OK;
+  const DeviceInfo* dev = current_device_info();
+  if (!dev) return FD_ERR_CUDA;
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  const Derived dv = derive(*a);
+  const int grid = grid_for(*a, dv, *dev);
+  const WorkspaceNeed need = workspace_need(*a, dv, grid);
+  if (need.scratch_bytes > 0 && (!a->scratch || a->scratch_bytes < need.scratch_bytes))
+    return FD_ERR_WORKSPACE;
+  if (need.tickets > 0 && (!a->tickets || a->tickets_capacity < need.tickets))
+    return FD_ERR_WORKSPACE;
+
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.num_seqs = a->num_seqs;
+  p.num_q_heads = a->num_q_heads;
+  p.num_kv_heads = a->num_kv_heads;
+  p.block_size = a->block_size;
+  p.num_blocks = a->num_blocks;
+  p.max_blocks = a->max_blocks_per_seq;
+  p.group = dv.group;
+  p.hb_per_kv = dv.hb_per_kv;
+  p.rows = dv.rows;
+  p.nhb = dv.nhb;
+  p.scale_log2 = a->sm_scale * kLog2e;
+  p.q = a->q;
+  p.qs0 = a->q_stride[0];
+  p.qs1 = a->q_stride[1];
+  p.qs2 = a->q_stride[2];
+  p.out = a->out;
+  p.os0 = a->out_stride[0];
+  p.os1 = a->out_stride[1];
+  p.os2 = a->out_stride[2];
+  p.k = a->k_cache;
+  p.ks0 = a->k_stride[0];
+  p.ks1 = a->k_stride[1];
+  p.ks2 = a->k_stride[2];
+  p.ks3 = a->k_stride[3];
+  p.v = a->v_cache;
+  p.vs0 = a->v_stride[0];
+  p.vs1 = a->v_stride[1];
+  p.vs2 = a->v_stride[2];
+  p.vs3 = a->v_stride[3];
+  p.bt = a->block_tables;
+  p.bt64 = a->block_tables_index == FD_INDEX_I64;
+  p.bts0 = a->block_tables_stride[0];
+  p.bts1 = a->block_tables_stride[1];
+  p.sl = a->seq_lens;
+  p.sl64 = a->seq_lens_index == FD_INDEX_I64;
+  p.sls = a->seq_lens_stride;
+  p.fused_append = a->append_k != nullptr;
+  if (p.fused_append) {
+    p.ak = a->append_k;
+    p.aks0 = a->append_k_stride[0];
+    p.aks1 = a->append_k_stride[1];
+    p.aks2 = a->append_k_stride[2];
+    p.av = a->append_v;
+    p.avs0 = a->append_v_stride[0];
+    p.avs1 = a->append_v_stride[1];
+    p.avs2 = a->append_v_stride[2];
+    p.slot = a->slot_mapping;
+    p.slot64 = a->slot_mapping_index == FD_INDEX_I64;
+    p.slots = a->slot_mapping_stride;
+  }
+  p.num_splits = a->num_splits;
+  p.epilogue = a->epilogue;
+  p.min_tiles_per_cta = a->min_tiles_per_cta > 0 ? a->min_tiles_per_cta : 4;
+  p.tickets = a->tickets;
+  p.status = device_status_ptr();
+  if (!p.status) return FD_ERR_CUDA;
+
+  const int D = a->head_dim;
+  if (a->num_splits == 0) {
+    const int64_t slots = static_cast<int64_t>(grid) + static_cast<int64_t>(a->num_seqs) * dv.nhb;
+    p.slot_acc = a->scratch;
+    p.slot_m = a->scratch + slots * dv.rows * D;
+    p.slot_l = p.slot_m + slots * dv.rows;
+  } else if (a->num_splits > 1 || a->epilogue == FD_EPILOGUE_PARTIALS) {
+    if (a->part_acc) {
+      p.pacc = a->part_acc;
+      p.pas0 = a->part_acc_stride[0];
+      p.pas1 = a->part_acc_stride[1];
+      p.pas2 = a->part_acc_stride[2];
+      p.pas3 = a->part_acc_stride[3];
+      p.pmax = a->part_max;
+      p.psum = a->part_sum;
+      p.pss0 = a->part_stat_stride[0];
+      p.pss1 = a->part_stat_stride[1];
+      p.pss2 = a->part_stat_stride[2];
+    } else {
+      const int64_t S = a->num_splits;
+      p.pacc = a->scratch;
+      p.pas3 = 1;
+      p.pas2 = D;
+      p.pas1 = S * D;
+      p.pas0 = static_cast<int64_t>(a->num_q_heads) * S * D;
+      p.pmax = a->scratch + static_cast<int64_t>(a->num_seqs) * a->num_q_heads * S * D;
+      p.psum = p.pmax + static_cast<int64_t>(a->num_seqs) * a->num_q_heads * S;
+      p.pss2 = 1;
+      p.pss1 = S;
+      p.pss0 = static_cast<int64_t>(a->num_q_heads) * S;
+    }
+  }
+
+  // loader: TMA when both planes are expressible as tensor maps
+  CUtensorMap mk, mv;
+  std::memset(&mk, 0, sizeof(mk));
+  std::memset(&mv, 0, sizeof(mv));
+  bool tma = true;
+  for (int plane = 0; plane < 2 && tma; ++plane) {
+    CacheDesc cd;
+    cd.base = plane ? a->v_cache : a->k_cache;
+    cd.elem_bytes = 2;
+    cd.is_bf16 = a->dtype == FD_DTYPE_BF16;
+    cd.head_dim = D;
+    cd.block_size = a->block_size;
+    cd.num_heads = a->num_kv_heads;
+    cd.num_blocks = a->num_blocks;
+    const int64_t* st = plane ? a->v_stride : a->k_stride;
+    for (int i = 0; i < 4; ++i) cd.stride[i] = st[i];
+    if (cd.num_heads == 1) cd.stride[1] = cd.stride[0];  // size-1 axis: any legal stride
+    tma = get_cache_tensor_map(cd, plane ? &mv : &mk, plane ? p.vperm : p.kperm);
+  }
+
+  const int sched_ints = (a->num_splits == 0) ? (a->num_seqs + 1) : 0;
+  const size_t fixed = (D == 128 ? smem_bytes<128>(0, sched_ints) : smem_bytes<64>(0, sched_ints));
+  const size_t stage_bytes = (D == 128 ? Smem<128>::kStageBytes : Smem<64>::kStageBytes) + 20;
+  const size_t cap = static_cast<size_t>(dev->max_smem_optin);
+  if (fixed + 2 * stage_bytes > cap) return FD_ERR_UNSUPPORTED;  // batch too large for the schedule
+  int stages = static_cast<int>((cap - fixed) / stage_bytes);
+  stages = std::min(stages, kMaxStages);
+  // Tile i uses stage i % stages and is consumed by warp i % kConsumerWarps.
+  // With stages a multiple of the consumer-warp count every stage is always
+  // consumed by the same warp, so each warp waits on a stage's phases in
+  // order and a parity wait can never alias a phase one ring ahead.
+  stages -= stages % kConsumerWarps;
+  if (stages < kConsumerWarps) return FD_ERR_UNSUPPORTED;
+  p.num_stages = stages;
+  const size_t smem = D == 128 ? smem_bytes<128>(stages, sched_ints) : smem_bytes<64>(stages, sched_ints);
+
+  const bool bf16 = a->dtype == FD_DTYPE_BF16;
+  if (D == 128) {
+    return bf16 ? dispatch_tma<__nv_bfloat16, 128>(tma, p, mk, mv, grid, smem, *dev, stream)
+                : dispatch_tma<__half, 128>(tma, p, mk, mv, grid, smem, *dev, stream);
+  }
+  return bf16 ? dispatch_tma<__nv_bfloat16, 64>(tma, p, mk, mv, grid, smem, *dev, stream)
+              : dispatch_tma<__half, 64>(tma, p, mk, mv, grid, smem, *dev, stream);
+}
+
+extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_stream) {
+  if (!a || a->struct_size != static_cast<int32_t>(sizeof(fd_split_kv_reduce_args)))
+    return FD_ERR_INVALID_ARGUMENT;
+  if (a->dtype != FD_DTYPE_F16 && a->dtype != FD_DTYPE_BF16 && a->dtype != FD_DTYPE_F32)
+    return FD_ERR_UNSUPPORTED;
+  if (a->num_seqs < 0 || a->num_q_heads <= 0 || a->head_dim <= 0 || a->num_splits <= 0)
+    return FD_ERR_INVALID_ARGUMENT;
+  if (!a->part_acc || !a->part_max || !a->part_sum || !a->seq_lens || !a->out)
+    return FD_ERR_INVALID_ARGUMENT;
+  if (a->num_seqs == 0) return FD_OK;
+  ReduceParams p;
+  p.num_seqs = a->num_seqs;
+  p.num_q_heads = a->num_q_heads;
+  p.head_dim = a->head_dim;
+  p.num_splits = a->num_splits;
+  p.acc = a->part_acc;
+  p.as0 = a->part_acc_stride[0];
+  p.as1 = a->part_acc_stride[1];
+  p.as2 = a->part_acc_stride[2];
+  p.as3 = a->part_acc_stride[3];
+  p.mx = a->part_max;
+  p.sm = a->part_sum;
+  p.ss0 = a->part_stat_stride[0];
+  p.ss1 = a->part_stat_stride[1];
+  p.ss2 = a->part_stat_stride[2];
+  p.sl = a->seq_lens;
+  p.sl64 = a->seq_lens_index == FD_INDEX_I64;
+  p.sls = a->seq_lens_stride;
+  p.slot = a->slot_mapping;
+  p.slot64 = a->slot_mapping_index == FD_INDEX_I64;
+  p.slots = a->slot_mapping_stride;
+  p.out = a->out;
+  p.os0 = a->out_stride[0];
+  p.os1 = a->out_stride[1];
+  p.os2 = a->out_stride[2];
+  dim3 grid(a->num_seqs, a->num_q_heads);
+  const int threads = a->head_dim >= 128 ? 128 : 64;
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  switch (a->dtype) {
+    case FD_DTYPE_BF16:
+      split_reduce_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(p);
+      break;
+    case FD_DTYPE_F16:
+      split_reduce_kernel<__half><<<grid, threads, 0, stream>>>(p);
+      break;
+    default:
+      split_reduce_kernel<float><<<grid, threads, 0, stream>>>(p);
+  }
+  return cuda_status(cudaGetLastError());
+}

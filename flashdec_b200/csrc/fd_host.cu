@@ -1,0 +1,231 @@
+// Host helpers: device properties, tensor-map encoding/caching, status word,
+// error strings.
+#include <algorithm>
+#include <array>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cudaTypedefs.h>
+
+#include "../../include/flashdec_b200.h"
+#include "fd_host.h"
+
+// Device status word: bits FD_STATUS_* raised by kernels (bounded waits that
+// ran out, masked out-of-range block ids).  Read with fd_device_status.
+__device__ int fd_g_status_word;
+
+namespace fd {
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+DeviceInfo g_dev[kMaxDevices];
+int* g_status_ptr[kMaxDevices] = {nullptr};
+
+thread_local std::string g_last_cuda_error;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+void resolve_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+}
+
+struct MapKey {
+  const void* base;
+  int elem_bytes, is_bf16, head_dim, block_size, num_heads, num_blocks;
+  int64_t stride[4];
+  bool operator==(const MapKey& o) const {
+    return base == o.base && elem_bytes == o.elem_bytes && is_bf16 == o.is_bf16 &&
+           head_dim == o.head_dim &&
+           block_size == o.block_size && num_heads == o.num_heads &&
+           num_blocks == o.num_blocks && std::memcmp(stride, o.stride, sizeof(stride)) == 0;
+  }
+};
+
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  int perm[3];
+  uint64_t stamp;
+};
+
+std::mutex g_map_mu;
+std::vector<MapEntry> g_maps;
+uint64_t g_map_clock = 0;
+constexpr size_t kMapCacheSize = 64;
+
+}  // namespace
+
+const DeviceInfo* current_device_info() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.device < 0) {
+    int sms = 0, smem = 0, ma = 0, mi = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&ma, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&mi, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      return nullptr;
+    }
+    d.num_sms = sms;
+    d.max_smem_optin = smem;
+    d.cc_major = ma;
+    d.cc_minor = mi;
+    d.device = dev;
+  }
+  return &d;
+}
+
+int* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, fd_g_status_word) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return FD_OK;
+  g_last_cuda_error = cudaGetErrorString(e);
+  return FD_ERR_CUDA;
+}
+
+bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]) {
+  if (d.elem_bytes != 2 || d.stride[3] != 1) return false;
+  if (d.head_dim != 64 && d.head_dim != 128) return false;
+  if (reinterpret_cast<uintptr_t>(d.base) % 16 != 0) return false;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t bytes = d.stride[i] * d.elem_bytes;
+    if (bytes <= 0 || bytes % 16 != 0 || bytes >= (int64_t(1) << 40)) return false;
+  }
+  MapKey key{d.base, d.elem_bytes, d.is_bf16, d.head_dim, d.block_size, d.num_heads, d.num_blocks,
+             {d.stride[0], d.stride[1], d.stride[2], d.stride[3]}};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    for (auto& e : g_maps) {
+      if (e.key == key) {
+        e.stamp = ++g_map_clock;
+        *out = e.map;
+        std::copy(e.perm, e.perm + 3, perm);
+        return true;
+      }
+    }
+  }
+  resolve_encoder();
+  if (!g_encode) return false;
+
+  // outer axes: 0 token (box = block_size), 1 head (box 1), 2 block (box 1)
+  struct Axis {
+    int id;
+    uint64_t size;
+    uint64_t stride_bytes;
+    uint32_t box;
+  };
+  std::array<Axis, 3> ax = {{
+      {0, static_cast<uint64_t>(d.block_size), static_cast<uint64_t>(d.stride[2] * 2),
+       static_cast<uint32_t>(d.block_size)},
+      {1, static_cast<uint64_t>(d.num_heads), static_cast<uint64_t>(d.stride[1] * 2), 1u},
+      {2, static_cast<uint64_t>(d.num_blocks), static_cast<uint64_t>(d.stride[0] * 2), 1u},
+  }};
+  std::stable_sort(ax.begin(), ax.end(),
+                   [](const Axis& a, const Axis& b) { return a.stride_bytes < b.stride_bytes; });
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d.head_dim), ax[0].size, ax[1].size, ax[2].size};
+  cuuint64_t strides[3] = {ax[0].stride_bytes, ax[1].stride_bytes, ax[2].stride_bytes};
+  cuuint32_t box[4] = {64u, ax[0].box, ax[1].box, ax[2].box};
+  cuuint32_t estride[4] = {1u, 1u, 1u, 1u};
+  CUtensorMap map;
+  CUresult r = g_encode(&map,
+                        d.is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        4, const_cast<void*>(d.base),
+                        dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  int pm[3] = {ax[0].id, ax[1].id, ax[2].id};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    if (g_maps.size() >= kMapCacheSize) {
+      auto oldest = std::min_element(g_maps.begin(), g_maps.end(),
+                                     [](const MapEntry& a, const MapEntry& b) {
+                                       return a.stamp < b.stamp;
+                                     });
+      g_maps.erase(oldest);
+    }
+    MapEntry e;
+    e.key = key;
+    e.map = map;
+    std::copy(pm, pm + 3, e.perm);
+    e.stamp = ++g_map_clock;
+    g_maps.push_back(e);
+  }
+  *out = map;
+  std::copy(pm, pm + 3, perm);
+  return true;
+}
+
+}  // namespace fd
+
+extern "C" {
+
+const char* fd_error_string(int code) {
+  switch (code) {
+    case FD_OK:
+      return "ok";
+    case FD_ERR_INVALID_ARGUMENT:
+      return "invalid argument";
+    case FD_ERR_UNSUPPORTED:
+      return "unsupported configuration";
+    case FD_ERR_WORKSPACE:
+      return "workspace missing or too small";
+    case FD_ERR_CUDA:
+      return fd::g_last_cuda_error.empty() ? "CUDA error" : fd::g_last_cuda_error.c_str();
+    case FD_ERR_ALIGNMENT:
+      return "misaligned pointer or stride";
+    default:
+      return "unknown error";
+  }
+}
+
+int fd_version(void) { return 1; }
+
+int fd_num_sms(void) {
+  const fd::DeviceInfo* d = fd::current_device_info();
+  return d ? d->num_sms : 0;
+}
+
+int fd_device_status(int clear, int* status_out) {
+  int* p = fd::device_status_ptr();
+  if (!p || !status_out) return FD_ERR_INVALID_ARGUMENT;
+  int v = 0;
+  int rc = fd::cuda_status(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (rc) return rc;
+  *status_out = v;
+  if (clear) {
+    const int zero = 0;
+    rc = fd::cuda_status(cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  return rc;
+}
+
+}  // extern "C"

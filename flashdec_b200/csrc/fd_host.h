@@ -1,0 +1,50 @@
+// Host-side helpers shared by the FlashDec B200 entry points: per-device
+// properties, the tensor-map encoder (driver entry point resolved at run time,
+// no link-time libcuda dependency) and a small cache of encoded maps.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace fd {
+
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+};
+
+// Cached properties of the current device (thread-safe).
+const DeviceInfo* current_device_info();
+
+// Description of one paged cache plane for TMA: logical order
+// [block, head, token, dim] with element strides; dim stride must be 1.
+struct CacheDesc {
+  const void* base;
+  int elem_bytes;       // 2
+  int is_bf16;          // 1 bf16, 0 fp16
+  int head_dim;         // 64 / 128
+  int block_size;       // 8 / 16 / 32
+  int num_heads;
+  int num_blocks;
+  int64_t stride[4];    // block, head, token, dim (elements)
+};
+
+// Encode (or fetch from the cache) a 4-D tiled tensor map over `d` with a box
+// of [64 dims x block_size tokens x 1 head x 1 block] and 128B swizzle.
+// `perm[i]` receives which logical axis (0 token, 1 head, 2 block) is tensor
+// map dimension i+1 (outer dims sorted by ascending stride).
+// Returns false when the layout cannot be described by a tensor map.
+bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]);
+
+// FD_OK, or FD_ERR_CUDA with the message kept for fd_error_string.
+int cuda_status(cudaError_t e);
+
+// Device address of the status word of the current device (cached).
+int* device_status_ptr();
+
+}  // namespace fd
