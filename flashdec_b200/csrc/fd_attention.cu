@@ -52,6 +52,7 @@ constexpr int kMiscInts = 8;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kBarConsumers = 1;  // named barrier id for the consumer warps
+constexpr int kMergeBatch = 10;   // partials merged per register batch
 
 struct AttnParams {
   int num_seqs, num_q_heads, num_kv_heads, block_size, num_blocks, max_blocks;
@@ -82,6 +83,8 @@ struct AttnParams {
   int fused_append;
   int num_splits;  // 0 = length-balanced (stream-K) schedule
   int epilogue;    // FD_EPILOGUE_*
+  int balanced;    // split mode: equal tile ranges instead of cdiv chunks
+  int cap_tiles;   // tiles of a full block-table row (speculative prefetch)
   int min_tiles_per_cta;
   // split-mode partials [seq, q_head, split, dim] / [seq, q_head, split]
   float* pacc;
@@ -152,6 +155,7 @@ struct Segment {
 
 struct Sched {
   const int* prefix;  // smem, tiles prefix over sequences [num_seqs + 1]
+  const int* seqn;    // smem, attended tokens per sequence [num_seqs]
   int64_t U;          // total tiles of the batch
   int g;              // CTAs that own work (<= gridDim.x)
   int64_t x, hi;      // this CTA's cursor / end (stream-K)
@@ -175,6 +179,24 @@ __device__ __forceinline__ int find_seq(const int* prefix, int num_seqs, int nhb
   return lo;
 }
 
+// Tiles of split `split` out of `tiles`: equal ranges when p.balanced
+// (within one tile), else the reference's cdiv chunks (paged_decode.py:405-411).
+__device__ __forceinline__ void split_range(const AttnParams& p, int split, int tiles, int& t0,
+                                            int& t1) {
+  const int S = p.num_splits;
+  if (p.balanced) {
+    // (split + 1) * tiles < 2^32 for any block table a device can hold
+    t0 = static_cast<int>(static_cast<uint32_t>(split) * static_cast<uint32_t>(tiles) /
+                          static_cast<uint32_t>(S));
+    t1 = static_cast<int>(static_cast<uint32_t>(split + 1) * static_cast<uint32_t>(tiles) /
+                          static_cast<uint32_t>(S));
+  } else {
+    const int bps = (tiles + S - 1) / S;
+    t0 = min(split * bps, tiles);
+    t1 = min(t0 + bps, tiles);
+  }
+}
+
 __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Segment& s) {
   if (p.num_splits == 0) {
     if (sc.x >= sc.hi) return false;
@@ -194,26 +216,21 @@ __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Seg
     s.c_first = sc.owner(pair_start);
     s.nseg = sc.owner(pair_end - 1) - s.c_first + 1;
     s.part_slot = static_cast<int>(blockIdx.x) + b * p.nhb + hb;
-    s.n = seq_info(p, b).n;
+    s.n = sc.seqn[b];
     sc.x = seg_end;
     return true;
   }
   if (sc.done) return false;
   sc.done = 1;
+  // split schedule: grid = (splits, head blocks, sequences)
   const int S = p.num_splits;
-  const int pid = static_cast<int>(blockIdx.x) / S;
-  const int split = static_cast<int>(blockIdx.x) % S;
-  if (pid >= p.num_seqs * p.nhb) return false;
-  s.b = pid / p.nhb;
-  s.hb = pid % p.nhb;
+  const int split = static_cast<int>(blockIdx.x);
+  s.hb = static_cast<int>(blockIdx.y);
+  s.b = static_cast<int>(blockIdx.z);
   const SeqInfo si = seq_info(p, s.b);
   s.n = si.n;
   s.tiles = si.tiles;
-  const int bps = (si.tiles + S - 1) / S;
-  const int t0 = min(split * bps, si.tiles);
-  const int t1 = min(t0 + bps, si.tiles);
-  s.t0 = t0;
-  s.t1 = t1 > t0 ? t1 : t0;
+  split_range(p, split, si.tiles, s.t0, s.t1);
   s.whole = (S == 1) && p.epilogue == FD_EPILOGUE_FUSED;
   s.part_slot = split;
   s.nseg = S;
@@ -293,30 +310,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = tid & 31;
   volatile int* abort_flag = misc;
 
+  if (tid < NST) {  // one stage's barriers per thread
+    mbar_init(smem_u32(&full_bar[tid]), 1);
+    mbar_init(smem_u32(&empty_bar[tid]), 1);
+    fence_mbar_init();
+  }
   if (tid == 0) {
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(smem_u32(&full_bar[s]), 1);
-      mbar_init(smem_u32(&empty_bar[s]), 1);
-    }
     misc[0] = 0;
     misc[1] = 0;
-    fence_mbar_init();
   }
   if (kTma && warp == kConsumerWarps && lane == 0) {
     prefetch_tensormap(&tmap_k);
     prefetch_tensormap(&tmap_v);
   }
+  // Everything above touches no global memory and may overlap the previous
+  // kernel of the stream; from here on its writes (KV cache, q, metadata,
+  // the shared tickets) must be visible.
+  pdl_wait();
+  pdl_launch_dependents();
 
   // ---- schedule ----------------------------------------------------------
   Sched sc;
   sc.prefix = prefix;
+  int* seqn = prefix + p.num_seqs + 1;
+  sc.seqn = seqn;
   sc.U = 0;
   sc.g = 1;
   sc.x = sc.hi = 0;
   sc.done = 0;
   const bool streamk = (p.num_splits == 0);
   if (streamk) {
-    for (int b = tid; b < p.num_seqs; b += kThreads) prefix[b + 1] = seq_info(p, b).tiles;
+    for (int b = tid; b < p.num_seqs; b += kThreads) {
+      const SeqInfo si = seq_info(p, b);
+      prefix[b + 1] = si.tiles;
+      seqn[b] = si.n;
+    }
     if (tid == 0) prefix[0] = 0;
   }
   __syncthreads();
@@ -353,111 +381,163 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int bs = p.block_size;
   const int PPT = kTile / bs;  // pages per tile: 1, 2 or 4
+  // Per-tile index math uses shifts and incrementally tracked (stage, phase)
+  // pairs: runtime division is a long dependent instruction sequence.
+  const int ppt_shift = bs == 32 ? 0 : (bs == 16 ? 1 : 2);
+  const int bs_shift = 5 - ppt_shift;  // log2(block_size)
 
   // =========================================================================
-  // producer warp
+  // producer warp.  Tiles are produced in groups of TG tiles (TG * PPT <= 32
+  // pages, TG <= NST / 2 so a group only waits on stages freed by earlier
+  // groups).  Lane j resolves the block id of page j of the group; lane i
+  // (< group tiles) waits on its tile's "empty" barrier and posts the byte
+  // count on the tile's "full" barrier; then all lanes issue the group's TMA
+  // boxes together.  One warp instruction thus covers many tiles instead of
+  // one lane walking tile by tile.
   // =========================================================================
   if (warp == kConsumerWarps) {
     const uint64_t policy = l2_policy_evict_first();
-    uint32_t iter = 0;
+    const int TG = max(1, min(32 >> ppt_shift, NST / 2));
+    constexpr int kOps = 2 * SM::kHalves;  // boxes per page: K and V halves
+    // (stage, phase parity) of the next tile to produce; a group of
+    // ntile <= NST / 2 tiles wraps the ring at most once.
+    int pst = 0;
+    uint32_t pph = 0;
+    auto stage_of = [&](int i, uint32_t& ph) {
+      int st = pst + i;
+      ph = pph;
+      if (st >= NST) {
+        st -= NST;
+        ph ^= 1u;
+      }
+      return st;
+    };
+    bool bad = false;
+    // Block-table window: lane l holds the entry of page wb + l (win) and of
+    // page wb + 32 + l (win_next, prefetched); win_b is the sequence.
+    int64_t wb = -1;
+    int win_b = -1, win = -1, win_next = -1;
+    auto bt_entry = [&](int b, int64_t lb) -> int {
+      return lb < p.max_blocks
+                 ? static_cast<int>(load_index(p.bt, p.bt64,
+                                               static_cast<int64_t>(b) * p.bts0 + lb * p.bts1))
+                 : -1;
+    };
+    if (!streamk) {
+      // Split schedule: this CTA's pair and (for a full-length sequence) its
+      // pages are known from blockIdx alone, so the first window is fetched
+      // speculatively, in parallel with the sequence-length load.
+      int st0, st1;
+      split_range(p, static_cast<int>(blockIdx.x), p.cap_tiles, st0, st1);
+      win_b = static_cast<int>(blockIdx.z);
+      wb = static_cast<int64_t>(st0) << ppt_shift;
+      win = bt_entry(win_b, wb + lane);
+      win_next = bt_entry(win_b, wb + 32 + lane);
+    }
     Segment s;
     while (next_segment(p, sc, s)) {
       if (s.t1 <= s.t0) continue;
       const int kv_head = s.hb / p.hb_per_kv;
       const int limit_cache = p.fused_append ? s.n - 1 : s.n;  // tokens read from the cache
-      const int nlb = (limit_cache + bs - 1) / bs;              // pages holding them
-      const int64_t lb_begin = static_cast<int64_t>(s.t0) * PPT;
-      const int64_t lb_end = min(static_cast<int64_t>(s.t1) * PPT, static_cast<int64_t>(nlb));
-      const char* bt_row = static_cast<const char*>(p.bt);
-      auto load_entry = [&](int64_t lb) -> int {
-        if (lb >= lb_end) return -1;
-        return static_cast<int>(
-            load_index(p.bt, p.bt64, static_cast<int64_t>(s.b) * p.bts0 + lb * p.bts1));
-      };
-      (void)bt_row;
-      int64_t chunk_base = lb_begin;
-      int cur = load_entry(chunk_base + lane);
-      int nxt = load_entry(chunk_base + 32 + lane);
-      bool bad = false;
-      for (int t = s.t0; t < s.t1; ++t, ++iter) {
-        const int stage = static_cast<int>(iter % NST);
-        const uint32_t phase = (iter / NST) & 1u;
-        const bool ok = mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.status, abort_flag);
-        uint32_t mask = 0;
-        int blk_of[4] = {-1, -1, -1, -1};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (j < PPT) {
-            const int64_t lb = static_cast<int64_t>(t) * PPT + j;
-            while (lb >= chunk_base + 32) {  // warp-uniform
-              chunk_base += 32;
-              cur = nxt;
-              nxt = load_entry(chunk_base + 32 + lane);
-            }
-            const int blk = __shfl_sync(0xffffffffu, cur, static_cast<int>(lb - chunk_base));
-            if (lb < lb_end) {
-              if (blk >= 0 && blk < p.num_blocks) {
-                mask |= 1u << j;
-                blk_of[j] = blk;
-              } else {
-                bad = true;
+      const int64_t nlb = (limit_cache + bs - 1) >> bs_shift;  // pages holding them
+      for (int tg = s.t0; tg < s.t1;) {
+        const int64_t pg0 = static_cast<int64_t>(tg) << ppt_shift;
+        if (win_b != s.b || pg0 < wb || pg0 >= wb + 64) {
+          wb = pg0;  // (re)load the window at this group
+          win_b = s.b;
+          win = bt_entry(s.b, wb + lane);
+          win_next = bt_entry(s.b, wb + 32 + lane);
+        } else if (pg0 >= wb + 32) {
+          wb += 32;  // slide by one window; prefetch the following one
+          win = win_next;
+          win_next = bt_entry(s.b, wb + 32 + lane);
+        }
+        // a group never crosses the window end
+        const int room = static_cast<int>((wb + 32 - pg0) >> ppt_shift);
+        const int ntile = min(min(TG, s.t1 - tg), room);
+        const int npage = ntile << ppt_shift;
+        const int64_t lb = pg0 + lane;
+        const bool has_tokens = lane < npage && lb < nlb;
+        int blk = __shfl_sync(0xffffffffu, win, static_cast<int>(pg0 - wb + lane) & 31);
+        if (!has_tokens) blk = -1;
+        const bool pvalid = has_tokens && blk >= 0 && blk < p.num_blocks;
+        bad = bad || (has_tokens && !pvalid);
+        const uint32_t pages = __ballot_sync(0xffffffffu, pvalid);
+        bool ok = true;
+        if (lane < ntile) {
+          uint32_t ph;
+          const int stage = stage_of(lane, ph);
+          ok = mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1u, p.status, abort_flag);
+          const uint32_t tmask = (pages >> (lane << ppt_shift)) & ((1u << PPT) - 1u);
+          stage_mask[stage] = tmask;
+          if (kTma && ok) {
+            mbar_arrive_expect_tx(smem_u32(&full_bar[stage]),
+                                  static_cast<uint32_t>(__popc(tmask)) * (bs * D * 2 * 2));
+          }
+        }
+        if (__all_sync(0xffffffffu, ok)) {
+          if constexpr (kTma) {
+            const int nops = npage * kOps;
+            for (int base = 0; base < nops; base += 32) {
+              const int op = base + lane;
+              const int page = op / kOps;  // kOps is a compile-time power of two
+              const int pblk = __shfl_sync(0xffffffffu, blk, page & 31);
+              if (op < nops && ((pages >> page) & 1u)) {
+                const int rem = op - page * kOps;
+                const int plane = rem / SM::kHalves;  // 0: K, 1: V
+                const int h = rem - plane * SM::kHalves;
+                const int ti = page >> ppt_shift;
+                const int j = page & (PPT - 1);
+                uint32_t ph;
+                const int stage = stage_of(ti, ph);
+                const uint32_t dst = smem_u32(stages + stage * SM::kStageBytes) +
+                                     plane * (SM::kHalves * SM::kHalfBytes) + h * SM::kHalfBytes +
+                                     ((j * bs) << 7);
+                const int* perm = plane ? p.vperm : p.kperm;
+                tma_load_4d(dst, plane ? &tmap_v : &tmap_k, smem_u32(&full_bar[stage]), h * 64,
+                            tmap_coord(perm[0], kv_head, pblk), tmap_coord(perm[1], kv_head, pblk),
+                            tmap_coord(perm[2], kv_head, pblk), policy);
               }
+            }
+          } else {
+            // generic strides: the producer warp copies the valid pages itself
+            for (int page = 0; page < npage; ++page) {
+              const int pblk = __shfl_sync(0xffffffffu, blk, page);
+              if (!((pages >> page) & 1u)) continue;
+              const int ti = page >> ppt_shift;
+              const int j = page & (PPT - 1);
+              uint32_t ph;
+              uint8_t* sb = stages + stage_of(ti, ph) * SM::kStageBytes;
+              const uint16_t* kp =
+                  static_cast<const uint16_t*>(p.k) + pblk * p.ks0 + kv_head * p.ks1;
+              const uint16_t* vp =
+                  static_cast<const uint16_t*>(p.v) + pblk * p.vs0 + kv_head * p.vs1;
+              for (int e = lane; e < bs * D; e += 32) {
+                const int r = e / D;
+                const int d = e - r * D;
+                const uint32_t off = tile_offset(j * bs + r, d);
+                *reinterpret_cast<uint16_t*>(sb + off) = kp[r * p.ks2 + d * p.ks3];
+                *reinterpret_cast<uint16_t*>(sb + SM::kHalves * SM::kHalfBytes + off) =
+                    vp[r * p.vs2 + d * p.vs3];
+              }
+            }
+            __syncwarp();
+            if (lane < ntile) {
+              uint32_t ph;
+              mbar_arrive(smem_u32(&full_bar[stage_of(lane, ph)]));
             }
           }
         }
-        if (!ok) continue;
-        const uint32_t sbase = smem_u32(stages + stage * SM::kStageBytes);
-        if constexpr (kTma) {
-          if (lane == 0) {
-            stage_mask[stage] = mask;
-            const uint32_t bytes = __popc(mask) * bs * D * 2 * 2;
-            const uint32_t fb = smem_u32(&full_bar[stage]);
-            mbar_arrive_expect_tx(fb, bytes);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (mask & (1u << j)) {
-                const int blk = blk_of[j];
-#pragma unroll
-                for (int h = 0; h < SM::kHalves; ++h) {
-                  const uint32_t off = h * SM::kHalfBytes + j * bs * 128;
-                  tma_load_4d(sbase + off, &tmap_k, fb, h * 64,
-                              tmap_coord(p.kperm[0], kv_head, blk),
-                              tmap_coord(p.kperm[1], kv_head, blk),
-                              tmap_coord(p.kperm[2], kv_head, blk), policy);
-                  tma_load_4d(sbase + SM::kHalves * SM::kHalfBytes + off, &tmap_v, fb, h * 64,
-                              tmap_coord(p.vperm[0], kv_head, blk),
-                              tmap_coord(p.vperm[1], kv_head, blk),
-                              tmap_coord(p.vperm[2], kv_head, blk), policy);
-                }
-              }
-            }
-          }
-        } else {
-          // generic strides: the producer warp copies the valid pages itself
-          uint8_t* sb = stages + stage * SM::kStageBytes;
-          for (int j = 0; j < PPT; ++j) {
-            if (!(mask & (1u << j))) continue;
-            const int blk = blk_of[j];
-            const uint16_t* kp = static_cast<const uint16_t*>(p.k) + blk * p.ks0 + kv_head * p.ks1;
-            const uint16_t* vp = static_cast<const uint16_t*>(p.v) + blk * p.vs0 + kv_head * p.vs1;
-            for (int e = lane; e < bs * D; e += 32) {
-              const int r = e / D;
-              const int d = e - r * D;
-              const uint32_t off = tile_offset(j * bs + r, d);
-              *reinterpret_cast<uint16_t*>(sb + off) = kp[r * p.ks2 + d * p.ks3];
-              *reinterpret_cast<uint16_t*>(sb + SM::kHalves * SM::kHalfBytes + off) =
-                  vp[r * p.vs2 + d * p.vs3];
-            }
-          }
-          __syncwarp();
-          if (lane == 0) {
-            stage_mask[stage] = mask;
-            mbar_arrive(smem_u32(&full_bar[stage]));
-          }
+        // (aborted groups are skipped; the consumers' waits then time out too)
+        pst += ntile;
+        if (pst >= NST) {
+          pst -= NST;
+          pph ^= 1u;
         }
+        tg += ntile;
       }
-      if (bad && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
     }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
     return;
   }
 
@@ -468,34 +548,64 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t4 = lane & 3;   // thread in group
   const int mi = lane >> 3;  // ldmatrix matrix index
   const int r8 = lane & 7;   // ldmatrix row
-  uint32_t iter = 0;
+  uint32_t iter = 0;  // tile counter (tile i is consumed by warp i % 4)
+  int cst = 0;        // (stage, phase parity) of tile `iter`
+  uint32_t cph = 0;
+  // ---- Q fragments (A operand, rows = query heads of the head block) ----
+  uint32_t qf[D / 16][4];
+  int q_b = -1, q_hb = -1;
+  // Q of the head block is staged into shared memory (the merge buffer, idle
+  // at a segment start) with 16-byte loads, in the swizzled tile layout, and
+  // read back as mma A fragments with ldmatrix.  Called by all consumer
+  // warps together.
+  auto load_q = [&](int b, int hb) {
+    const int kvh = hb / p.hb_per_kv;
+    const int jb = hb % p.hb_per_kv;
+    const int h0 = kvh * p.group + jb * p.rows;
+    const int nr = min(p.rows, p.group - jb * p.rows);
+    const T* qb = static_cast<const T*>(p.q) + b * p.qs0;
+    uint8_t* qs = reinterpret_cast<uint8_t*>(obuf);
+    for (int c = tid; c < kMaxRows * (D / 8); c += kConsumerThreads) {
+      const int row = c / (D / 8);
+      const int ch = c - row * (D / 8);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (row < nr) {
+        const T* src = qb + (h0 + row) * p.qs1 + ch * 8 * p.qs2;
+        if (p.qs2 == 1 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+          v = *reinterpret_cast<const uint4*>(src);
+        } else {
+          __align__(16) T e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) e[i] = src[i * p.qs2];
+          v = *reinterpret_cast<const uint4*>(e);
+        }
+      }
+      *reinterpret_cast<uint4*>(qs + chunk_offset(row, ch)) = v;
+    }
+    named_barrier(kBarConsumers, kConsumerThreads);
+    const uint32_t qbase = smem_u32(qs);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      ldsm_x4(qbase + chunk_offset(r8 + (mi & 1) * 8, ks * 2 + (mi >> 1)), qf[ks][0], qf[ks][1],
+              qf[ks][2], qf[ks][3]);
+    }
+    named_barrier(kBarConsumers, kConsumerThreads);
+    q_b = b;
+    q_hb = hb;
+  };
+  if (!streamk) {
+    // split schedule: the pair is known from blockIdx; load Q before the
+    // sequence length arrives
+    load_q(static_cast<int>(blockIdx.z), static_cast<int>(blockIdx.y));
+  }
+
   Segment s;
   while (next_segment(p, sc, s)) {
     const int kv_head = s.hb / p.hb_per_kv;
     const int jblk = s.hb % p.hb_per_kv;
     const int head0 = kv_head * p.group + jblk * p.rows;
     const int nrows = min(p.rows, p.group - jblk * p.rows);
-
-    // ---- Q fragments (A operand, rows = query heads) ----
-    uint32_t qf[D / 16][4];
-    {
-      const T* qb = static_cast<const T*>(p.q) + s.b * p.qs0;
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          const int row = g8 + ((rr & 1) ? 8 : 0);
-          const int d = ks * 16 + 2 * t4 + ((rr & 2) ? 8 : 0);
-          float a = 0.f, c = 0.f;
-          if (row < nrows) {
-            const T* qr = qb + (head0 + row) * p.qs1;
-            a = to_f32<T>(qr[d * p.qs2]);
-            c = to_f32<T>(qr[(d + 1) * p.qs2]);
-          }
-          qf[ks][rr] = pack2<T>(a, c);
-        }
-      }
-    }
+    if (s.b != q_b || s.hb != q_hb) load_q(s.b, s.hb);
 
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float o[D / 8][4];
@@ -503,10 +613,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
     const int limit_cache = p.fused_append ? s.n - 1 : s.n;
-    for (int t = s.t0; t < s.t1; ++t, ++iter) {
-      if (static_cast<int>(iter % kConsumerWarps) != warp) continue;
-      const int stage = static_cast<int>(iter % NST);
-      const uint32_t phase = (iter / NST) & 1u;
+    for (int t = s.t0; t < s.t1; ++t) {
+      const int stage = cst;
+      const uint32_t phase = cph;
+      const bool mine = static_cast<int>(iter & (kConsumerWarps - 1)) == warp;
+      ++iter;
+      if (++cst == NST) {
+        cst = 0;
+        cph ^= 1u;
+      }
+      if (!mine) continue;
       if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, abort_flag)) continue;
       uint8_t* sb = stages + stage * SM::kStageBytes;
       const uint32_t kbase = smem_u32(sb);
@@ -516,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // valid rows of this tile
       const int pos = base + lane;
-      const bool from_cache = pos < limit_cache && ((pmask >> (lane / bs)) & 1u);
+      const bool from_cache = pos < limit_cache && ((pmask >> (lane >> bs_shift)) & 1u);
       const bool appended = p.fused_append && pos == s.n - 1;
       const uint32_t vmask = __ballot_sync(0xffffffffu, from_cache || appended);
       bool touched = false;
@@ -541,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const T* akp = static_cast<const T*>(p.ak) + s.b * p.aks0 + kv_head * p.aks1;
         const T* avp = static_cast<const T*>(p.av) + s.b * p.avs0 + kv_head * p.avs1;
         const int64_t slot = load_index(p.slot, p.slot64, static_cast<int64_t>(s.b) * p.slots);
-        const int64_t sblk = slot / bs;
+        const int64_t sblk = slot >> bs_shift;
         const int64_t soff = slot - sblk * bs;
         const bool store = (jblk == 0) && sblk < p.num_blocks;
         T* kc = static_cast<T*>(p.k) + sblk * p.ks0 + kv_head * p.ks1 + soff * p.ks2;
@@ -694,10 +810,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         PartRef<D> pr = part_ref<D>(p, s, s.part_slot, r, head0 + r);
         float* ap = pr.acc + d * pr.acc_step_d;
-        ap[0] = a0;
-        ap[pr.acc_step_d] = a1;
-        ap[2 * pr.acc_step_d] = a2;
-        ap[3 * pr.acc_step_d] = a3;
+        if (pr.acc_step_d == 1 && (reinterpret_cast<uintptr_t>(ap) & 15u) == 0) {
+          *reinterpret_cast<float4*>(ap) = make_float4(a0, a1, a2, a3);
+        } else {
+          ap[0] = a0;
+          ap[pr.acc_step_d] = a1;
+          ap[2 * pr.acc_step_d] = a2;
+          ap[3 * pr.acc_step_d] = a3;
+        }
         if (d == 0) {
           *pr.m = (M == -INFINITY) ? -INFINITY : M * kLn2;  // natural-log units
           *pr.l = L;
@@ -705,45 +825,102 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (!s.whole && p.epilogue == FD_EPILOGUE_FUSED) {
-      __threadfence();
+      // The barrier orders every consumer thread's partial stores before
+      // thread 0's acq_rel ticket, which publishes them at GPU scope
+      // (release) and, for the last arriver, makes the other CTAs' partials
+      // visible (acquire); the second barrier extends that to all threads.
       named_barrier(kBarConsumers, kConsumerThreads);
       if (tid == 0) {
-        const int prev = atomicAdd(&p.tickets[pid], 1);
+        const int prev = atom_add_acq_rel_gpu(&p.tickets[pid], 1);
         const int last = (prev == s.nseg - 1);
-        if (last) atomicExch(&p.tickets[pid], 0);  // re-arm for the next call
+        // Re-arm for the next call: every contributor has arrived, nothing
+        // else touches this ticket before the kernel ends.
+        if (last) p.tickets[pid] = 0;
         misc[1] = last;
       }
       named_barrier(kBarConsumers, kConsumerThreads);
       if (misc[1]) {
-        __threadfence();
-        // final merge of the pair's nseg partials (reference reducer
-        // semantics, paged_decode.py:593-635)
-        for (int e = tid; e < nrows * (D / 4); e += kConsumerThreads) {
-          const int r = e / (D / 4);
-          const int d = (e - r * (D / 4)) * 4;
-          float M = -INFINITY;
-          for (int i = 0; i < s.nseg; ++i) {
-            const int sl = (p.num_splits == 0) ? (s.c_first + i + pid) : i;
-            M = fmaxf(M, __ldcg(part_ref<D>(p, s, sl, r, head0 + r).m));
+        // Final merge of the pair's nseg partials (reference reducer
+        // semantics, paged_decode.py:593-635).  One warp per output row, one
+        // lane per 4 dims (D/4 lanes); the (max, sum, acc) of up to
+        // kMergeBatch partials are loaded into registers by a fully unrolled,
+        // predicated loop -- all independent, so one memory round trip --
+        // and merged afterwards.
+        constexpr int kLanesPerRow = D / 4;
+        constexpr int kRowsPerWarp = 32 / kLanesPerRow;  // 1 (D=128) or 2 (D=64)
+        constexpr int kSlots = kConsumerWarps * kRowsPerWarp;
+        constexpr int kRowPass = 2;  // rows a lane merges together (loads overlap)
+        const int sub = lane / kLanesPerRow;
+        const int d = (lane - sub * kLanesPerRow) * 4;
+        for (int r0 = warp * kRowsPerWarp + sub; r0 < nrows; r0 += kSlots * kRowPass) {
+          float M[kRowPass], L[kRowPass], A[kRowPass][4];
+#pragma unroll
+          for (int q = 0; q < kRowPass; ++q) {
+            M[q] = -INFINITY;
+            L[q] = 0.f;
+            A[q][0] = A[q][1] = A[q][2] = A[q][3] = 0.f;
           }
-          float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-          if (M != -INFINITY) {
-            for (int i = 0; i < s.nseg; ++i) {
-              const int sl = (p.num_splits == 0) ? (s.c_first + i + pid) : i;
-              PartRef<D> pr = part_ref<D>(p, s, sl, r, head0 + r);
-              const float mi_ = __ldcg(pr.m);
-              if (mi_ == -INFINITY) continue;
-              const float wgt = exp2f((mi_ - M) * kLog2e);
-              L += wgt * __ldcg(pr.l);
-              const float* ap = pr.acc + d * pr.acc_step_d;
-              a0 += wgt * __ldcg(ap);
-              a1 += wgt * __ldcg(ap + pr.acc_step_d);
-              a2 += wgt * __ldcg(ap + 2 * pr.acc_step_d);
-              a3 += wgt * __ldcg(ap + 3 * pr.acc_step_d);
+          for (int i0 = 0; i0 < s.nseg; i0 += kMergeBatch) {
+            float mv[kRowPass][kMergeBatch], lv[kRowPass][kMergeBatch];
+            float4 av[kRowPass][kMergeBatch];
+#pragma unroll
+            for (int q = 0; q < kRowPass; ++q) {
+              const int r = r0 + q * kSlots;
+#pragma unroll
+              for (int j = 0; j < kMergeBatch; ++j) {
+                mv[q][j] = -INFINITY;
+                lv[q][j] = 0.f;
+                av[q][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                const int i = i0 + j;
+                if (r < nrows && i < s.nseg) {
+                  const int sl = (p.num_splits == 0) ? (s.c_first + i + pid) : i;
+                  const PartRef<D> pr = part_ref<D>(p, s, sl, r, head0 + r);
+                  mv[q][j] = __ldcg(pr.m);
+                  lv[q][j] = __ldcg(pr.l);
+                  const float* ap = pr.acc + d * pr.acc_step_d;
+                  if (pr.acc_step_d == 1 && (reinterpret_cast<uintptr_t>(ap) & 15u) == 0) {
+                    av[q][j] = __ldcg(reinterpret_cast<const float4*>(ap));
+                  } else {
+                    av[q][j] = make_float4(__ldcg(ap), __ldcg(ap + pr.acc_step_d),
+                                           __ldcg(ap + 2 * pr.acc_step_d),
+                                           __ldcg(ap + 3 * pr.acc_step_d));
+                  }
+                }
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < kRowPass; ++q) {
+              float Mn = M[q];
+#pragma unroll
+              for (int j = 0; j < kMergeBatch; ++j) Mn = fmaxf(Mn, mv[q][j]);
+              if (Mn == -INFINITY) continue;  // only empty splits so far
+              const float sa = exp2f((M[q] - Mn) * kLog2e);  // 0 while M is -inf
+              L[q] *= sa;
+              A[q][0] *= sa;
+              A[q][1] *= sa;
+              A[q][2] *= sa;
+              A[q][3] *= sa;
+#pragma unroll
+              for (int j = 0; j < kMergeBatch; ++j) {
+                const float w = exp2f((mv[q][j] - Mn) * kLog2e);  // 0 for empty splits
+                L[q] += w * lv[q][j];
+                A[q][0] += w * av[q][j].x;
+                A[q][1] += w * av[q][j].y;
+                A[q][2] += w * av[q][j].z;
+                A[q][3] += w * av[q][j].w;
+              }
+              M[q] = Mn;
             }
           }
-          const float inv = L > 0.f ? 1.f / L : 0.f;
-          store_out4<T>(p, s.b, head0 + r, d, a0 * inv, a1 * inv, a2 * inv, a3 * inv);
+#pragma unroll
+          for (int q = 0; q < kRowPass; ++q) {
+            const int r = r0 + q * kSlots;
+            if (r < nrows) {
+              const float inv = L[q] > 0.f ? 1.f / L[q] : 0.f;
+              store_out4<T>(p, s.b, head0 + r, d, A[q][0] * inv, A[q][1] * inv, A[q][2] * inv,
+                            A[q][3] * inv);
+            }
+          }
         }
       }
     }
@@ -791,6 +968,8 @@ struct ReduceParams {
 
 template <typename T>
 __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   const int h = blockIdx.y;
   const int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
@@ -861,15 +1040,52 @@ int validate(const fd_paged_decode_args* a) {
   if (a->epilogue != FD_EPILOGUE_FUSED && a->epilogue != FD_EPILOGUE_PARTIALS)
     return FD_ERR_INVALID_ARGUMENT;
   if (a->epilogue == FD_EPILOGUE_PARTIALS && a->num_splits == 0) return FD_ERR_INVALID_ARGUMENT;
+  if (a->num_splits > 0 && a->num_seqs > 65535) return FD_ERR_UNSUPPORTED;  // grid.z limit
   return FD_OK;
 }
 
-int grid_for(const fd_paged_decode_args& a, const Derived& dv, const DeviceInfo& dev) {
-  if (a.num_splits == 0) {
-    int g = a.max_ctas > 0 ? a.max_ctas : dev.num_sms;
-    return g < 1 ? 1 : g;
+// Launch plan.  An explicit num_splits keeps the reference's fixed split.
+// Automatic (num_splits == 0):
+//   * few (sequence, head block) pairs and short block tables -- the
+//     latency regime of small decode batches -- every pair gets
+//     S = SMs / pairs CTAs with equal tile ranges, so each CTA owns one
+//     segment and knows its pages from blockIdx alone;
+//   * otherwise (or when max_ctas is given) the persistent length-balanced
+//     schedule over the whole batch.
+constexpr int kSplitMaxTilesPerCta = 32;
+constexpr int kSplitMinTilesPerCta = 2;
+
+struct Plan {
+  int splits;    // 0: length-balanced persistent schedule
+  int balanced;
+  int grid;
+  int cap_tiles;
+};
+
+Plan make_plan(const fd_paged_decode_args& a, const Derived& dv, const DeviceInfo& dev) {
+  Plan pl;
+  const int64_t pairs = static_cast<int64_t>(a.num_seqs) * dv.nhb;
+  const int64_t cap_tokens = static_cast<int64_t>(a.max_blocks_per_seq) * a.block_size;
+  pl.cap_tiles = static_cast<int>((cap_tokens + kTile - 1) / kTile);
+  pl.balanced = 0;
+  if (a.num_splits > 0) {
+    pl.splits = a.num_splits;
+    pl.grid = static_cast<int>(pairs * a.num_splits);
+    return pl;
   }
-  return a.num_seqs * dv.nhb * a.num_splits;
+  const int64_t nsm = dev.num_sms;
+  if (a.max_ctas <= 0 && pairs <= nsm && pairs * pl.cap_tiles <= nsm * kSplitMaxTilesPerCta) {
+    int64_t s = nsm / pairs;
+    s = std::min<int64_t>(s, std::max(1, pl.cap_tiles / kSplitMinTilesPerCta));
+    pl.splits = static_cast<int>(std::max<int64_t>(1, s));
+    pl.balanced = 1;
+    pl.grid = static_cast<int>(pairs * pl.splits);
+    return pl;
+  }
+  pl.splits = 0;
+  const int g = a.max_ctas > 0 ? a.max_ctas : dev.num_sms;
+  pl.grid = g < 1 ? 1 : g;
+  return pl;
 }
 
 struct WorkspaceNeed {
@@ -877,26 +1093,26 @@ struct WorkspaceNeed {
   int64_t tickets = 0;
 };
 
-WorkspaceNeed workspace_need(const fd_paged_decode_args& a, const Derived& dv, int grid) {
+WorkspaceNeed workspace_need(const fd_paged_decode_args& a, const Derived& dv, const Plan& pl) {
   WorkspaceNeed w;
   const int64_t pairs = static_cast<int64_t>(a.num_seqs) * dv.nhb;
-  if (a.num_splits == 0) {
-    const int64_t slots = static_cast<int64_t>(grid) + pairs;
+  if (pl.splits == 0) {
+    const int64_t slots = static_cast<int64_t>(pl.grid) + pairs;
     w.scratch_bytes = static_cast<size_t>(slots) * dv.rows * (a.head_dim + 2) * sizeof(float);
     w.tickets = pairs;
   } else {
-    const bool partials = a.num_splits > 1 || a.epilogue == FD_EPILOGUE_PARTIALS;
+    const bool partials = pl.splits > 1 || a.epilogue == FD_EPILOGUE_PARTIALS;
     if (partials && !a.part_acc) {
-      w.scratch_bytes = static_cast<size_t>(a.num_seqs) * a.num_q_heads * a.num_splits *
+      w.scratch_bytes = static_cast<size_t>(a.num_seqs) * a.num_q_heads * pl.splits *
                         (a.head_dim + 2) * sizeof(float);
     }
-    if (a.num_splits > 1 && a.epilogue == FD_EPILOGUE_FUSED) w.tickets = pairs;
+    if (pl.splits > 1 && a.epilogue == FD_EPILOGUE_FUSED) w.tickets = pairs;
   }
   return w;
 }
 
 template <typename T, int D, bool kTma>
-int launch(const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv, int grid,
+int launch(const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
            size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
   auto kern = paged_decode_kernel<T, D, kTma>;
   static std::once_flag once[64];
@@ -907,13 +1123,22 @@ int launch(const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv, 
                                           dev.max_smem_optin);
   });
   if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
-  kern<<<grid, kThreads, smem, stream>>>(prm, mk, mv);
-  return cuda_status(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm, mk, mv));
 }
 
 template <typename T, int D>
 int dispatch_tma(bool tma, const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
-                 int grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
+                 dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
   return tma ? launch<T, D, true>(prm, mk, mv, grid, smem, dev, st)
              : launch<T, D, false>(prm, mk, mv, grid, smem, dev, st);
 }
@@ -930,7 +1155,7 @@ extern "C" int fd_paged_decode_workspace(const fd_paged_decode_args* a, size_t* 
   const DeviceInfo* dev = current_device_info();
   if (!dev) return FD_ERR_CUDA;
   const Derived dv = derive(*a);
-  const WorkspaceNeed w = workspace_need(*a, dv, grid_for(*a, dv, *dev));
+  const WorkspaceNeed w = workspace_need(*a, dv, make_plan(*a, dv, *dev));
   if (scratch_bytes) *scratch_bytes = w.scratch_bytes;
   if (tickets_needed) *tickets_needed = w.tickets;
   return FD_OK;
@@ -944,8 +1169,14 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
   if (!dev) return FD_ERR_CUDA;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   const Derived dv = derive(*a);
-  const int grid = grid_for(*a, dv, *dev);
-  const WorkspaceNeed need = workspace_need(*a, dv, grid);
+  const Plan plan = make_plan(*a, dv, *dev);
+  const int grid = plan.grid;
+  // split schedule: (split, head block, sequence) -- no division in-kernel
+  const dim3 gdim = plan.splits == 0 ? dim3(static_cast<unsigned>(grid))
+                                     : dim3(static_cast<unsigned>(plan.splits),
+                                            static_cast<unsigned>(dv.nhb),
+                                            static_cast<unsigned>(a->num_seqs));
+  const WorkspaceNeed need = workspace_need(*a, dv, plan);
   if (need.scratch_bytes > 0 && (!a->scratch || a->scratch_bytes < need.scratch_bytes))
     return FD_ERR_WORKSPACE;
   if (need.tickets > 0 && (!a->tickets || a->tickets_capacity < need.tickets))
@@ -1003,7 +1234,9 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
     p.slot64 = a->slot_mapping_index == FD_INDEX_I64;
     p.slots = a->slot_mapping_stride;
   }
-  p.num_splits = a->num_splits;
+  p.num_splits = plan.splits;
+  p.balanced = plan.balanced;
+  p.cap_tiles = plan.cap_tiles;
   p.epilogue = a->epilogue;
   p.min_tiles_per_cta = a->min_tiles_per_cta > 0 ? a->min_tiles_per_cta : 4;
   p.tickets = a->tickets;
@@ -1011,12 +1244,12 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
   if (!p.status) return FD_ERR_CUDA;
 
   const int D = a->head_dim;
-  if (a->num_splits == 0) {
+  if (plan.splits == 0) {
     const int64_t slots = static_cast<int64_t>(grid) + static_cast<int64_t>(a->num_seqs) * dv.nhb;
     p.slot_acc = a->scratch;
     p.slot_m = a->scratch + slots * dv.rows * D;
     p.slot_l = p.slot_m + slots * dv.rows;
-  } else if (a->num_splits > 1 || a->epilogue == FD_EPILOGUE_PARTIALS) {
+  } else if (plan.splits > 1 || a->epilogue == FD_EPILOGUE_PARTIALS) {
     if (a->part_acc) {
       p.pacc = a->part_acc;
       p.pas0 = a->part_acc_stride[0];
@@ -1029,7 +1262,7 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
       p.pss1 = a->part_stat_stride[1];
       p.pss2 = a->part_stat_stride[2];
     } else {
-      const int64_t S = a->num_splits;
+      const int64_t S = plan.splits;
       p.pacc = a->scratch;
       p.pas3 = 1;
       p.pas2 = D;
@@ -1063,7 +1296,7 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
     tma = get_cache_tensor_map(cd, plane ? &mv : &mk, plane ? p.vperm : p.kperm);
   }
 
-  const int sched_ints = (a->num_splits == 0) ? (a->num_seqs + 1) : 0;
+  const int sched_ints = (plan.splits == 0) ? (2 * a->num_seqs + 1) : 0;
   const size_t fixed = (D == 128 ? smem_bytes<128>(0, sched_ints) : smem_bytes<64>(0, sched_ints));
   const size_t stage_bytes = (D == 128 ? Smem<128>::kStageBytes : Smem<64>::kStageBytes) + 20;
   const size_t cap = static_cast<size_t>(dev->max_smem_optin);
@@ -1081,11 +1314,11 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
 
   const bool bf16 = a->dtype == FD_DTYPE_BF16;
   if (D == 128) {
-    return bf16 ? dispatch_tma<__nv_bfloat16, 128>(tma, p, mk, mv, grid, smem, *dev, stream)
-                : dispatch_tma<__half, 128>(tma, p, mk, mv, grid, smem, *dev, stream);
+    return bf16 ? dispatch_tma<__nv_bfloat16, 128>(tma, p, mk, mv, gdim, smem, *dev, stream)
+                : dispatch_tma<__half, 128>(tma, p, mk, mv, gdim, smem, *dev, stream);
   }
-  return bf16 ? dispatch_tma<__nv_bfloat16, 64>(tma, p, mk, mv, grid, smem, *dev, stream)
-              : dispatch_tma<__half, 64>(tma, p, mk, mv, grid, smem, *dev, stream);
+  return bf16 ? dispatch_tma<__nv_bfloat16, 64>(tma, p, mk, mv, gdim, smem, *dev, stream)
+              : dispatch_tma<__half, 64>(tma, p, mk, mv, gdim, smem, *dev, stream);
 }
 
 extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_stream) {
@@ -1128,13 +1361,11 @@ extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_s
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   switch (a->dtype) {
     case FD_DTYPE_BF16:
-      split_reduce_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(p);
-      break;
+      return cuda_status(launch_pdl(split_reduce_kernel<__nv_bfloat16>, grid, dim3(threads), 0,
+                                    stream, p));
     case FD_DTYPE_F16:
-      split_reduce_kernel<__half><<<grid, threads, 0, stream>>>(p);
-      break;
+      return cuda_status(launch_pdl(split_reduce_kernel<__half>, grid, dim3(threads), 0, stream, p));
     default:
-      split_reduce_kernel<float><<<grid, threads, 0, stream>>>(p);
+      return cuda_status(launch_pdl(split_reduce_kernel<float>, grid, dim3(threads), 0, stream, p));
   }
-  return cuda_status(cudaGetLastError());
 }

@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <array>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -102,6 +103,14 @@ int* device_status_ptr() {
     g_status_ptr[dev] = static_cast<int*>(p);
   }
   return g_status_ptr[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLASHDEC_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int cuda_status(cudaError_t e) {

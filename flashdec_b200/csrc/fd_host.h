@@ -47,4 +47,26 @@ int cuda_status(cudaError_t e);
 // Device address of the status word of the current device (cached).
 int* device_status_ptr();
 
+// Whether launches opt in to programmatic dependent launch (default on;
+// FLASHDEC_B200_PDL=0 turns it off).
+bool pdl_enabled();
+
+// Launch `kern` with the programmatic-stream-serialization attribute (the
+// kernel calls griddepcontrol.wait before touching global memory).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 }  // namespace fd

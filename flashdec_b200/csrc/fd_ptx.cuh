@@ -197,6 +197,22 @@ __device__ __forceinline__ int64_t load_index(const void* base, int is64, int64_
               : static_cast<int64_t>(static_cast<const int32_t*>(base)[i]);
 }
 
+// Programmatic dependent launch: allow the next kernel of the stream to be
+// scheduled, and wait until the previous one has completed and its memory is
+// visible.  No-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Atomic add at GPU scope with acquire-release semantics; returns the old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

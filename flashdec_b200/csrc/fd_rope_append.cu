@@ -67,6 +67,8 @@ __device__ __forceinline__ void rotate_row(const T* x, int64_t xs, T* y, int64_t
 
 template <typename T>
 __global__ void rope_kv_append_kernel(const __grid_constant__ RopeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warps_per_cta = blockDim.x >> 5;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -174,15 +176,13 @@ extern "C" int fd_rope_kv_append(const fd_rope_kv_append_args* a, void* cuda_str
   const int64_t grid = (rows + kWarps - 1) / kWarps;
   if (grid > 0x7fffffff) return FD_ERR_INVALID_ARGUMENT;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  const dim3 g(static_cast<unsigned>(grid)), blk(32 * kWarps);
   switch (a->dtype) {
     case FD_DTYPE_BF16:
-      rope_kv_append_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 32 * kWarps, 0, stream>>>(p);
-      break;
+      return cuda_status(launch_pdl(rope_kv_append_kernel<__nv_bfloat16>, g, blk, 0, stream, p));
     case FD_DTYPE_F16:
-      rope_kv_append_kernel<__half><<<static_cast<unsigned>(grid), 32 * kWarps, 0, stream>>>(p);
-      break;
+      return cuda_status(launch_pdl(rope_kv_append_kernel<__half>, g, blk, 0, stream, p));
     default:
-      rope_kv_append_kernel<float><<<static_cast<unsigned>(grid), 32 * kWarps, 0, stream>>>(p);
+      return cuda_status(launch_pdl(rope_kv_append_kernel<float>, g, blk, 0, stream, p));
   }
-  return cuda_status(cudaGetLastError());
 }
