@@ -252,7 +252,7 @@ def run_ours(args, rank, world, local_rank):
 
     # end to end through the public API: pinned host inputs, H2D, decode, D2H
     e2e = None
-    if rank == 0 or world > 1:
+    if not args.kernel_only:
         e2e_steps = min(args.steps, 3000)
         hq = [p["q"].cpu().pin_memory() for p in pools]
         hbt = [p["bt"].cpu().pin_memory() for p in pools]
@@ -302,7 +302,7 @@ def run_ours(args, rank, world, local_rank):
         }
 
     # ragged long-context batch, LPT-sharded over ranks
-    ragged = run_ragged(torch, dist, device, rank, world, stream, args)
+    ragged = None if args.kernel_only else run_ragged(torch, dist, device, rank, world, stream, args)
 
     if world > 1:
         dist.barrier()
@@ -311,7 +311,7 @@ def run_ours(args, rank, world, local_rank):
     nbytes = c2_bytes()
     peak, peak_kind = _peaks()
     achieved = nbytes / (ms_per_step / 1000.0) / 1e9
-    cpu = cpu_baseline_sample(args)
+    cpu = None if args.kernel_only else cpu_baseline_sample(args)
     return {
         "metric": METRIC,
         "value": world * C2["batch"] * args.steps / (max_ms / 1000.0),
@@ -525,6 +525,9 @@ def main():
     ap.add_argument("--steps", type=int, default=120000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the device-resident c2 step (no e2e, ragged or CPU "
+                         "legs); the small case used for ncu captures")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
