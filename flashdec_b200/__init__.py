@@ -18,6 +18,7 @@ __all__ = [
     "DecodeStepResult",
     "RopeAppendResult",
     "__version__",
+    "apply_rope",
     "cuda_kv_append",
     "decode",
     "fused_rope_kv_append",
@@ -45,7 +46,7 @@ def __getattr__(name):
         from . import cache
 
         return getattr(cache, name)
-    if name in ("RopeAppendResult", "rope_paged_kv_append"):
+    if name in ("RopeAppendResult", "apply_rope", "rope_paged_kv_append"):
         from . import rope
 
         return getattr(rope, name)

@@ -183,17 +183,16 @@ def split_kv_reduce(acc, mx, sm, seq_lens, out, *, num_seqs, slot_mapping=None):
 
 def rope_kv_append(q, q_out, k, v, k_cache4, v_cache4, block_ids, block_offsets, positions,
                    rotary_dim, inv_freq):
-    """Launch fd_rope_kv_append; q/q_out may be None (K/V only)."""
+    """Launch fd_rope_kv_append; q/q_out may be None (K/V only) and k may be
+    None (rotate q only: v, the caches and block ids/offsets are then unused)."""
     lib = _lib.load_library()
     a = _lib.RopeKVAppendArgs()
     a.struct_size = ctypes.sizeof(_lib.RopeKVAppendArgs)
-    a.dtype = dtype_code(k)
-    a.batch = k.shape[0]
-    a.num_kv_heads = k.shape[1]
-    a.head_dim = k.shape[2]
+    lead = k if k is not None else q
+    a.dtype = dtype_code(lead)
+    a.batch = lead.shape[0]
+    a.head_dim = lead.shape[2]
     a.rotary_dim = int(rotary_dim)
-    a.block_size = k_cache4.shape[2]
-    a.num_blocks = k_cache4.shape[0]
     if inv_freq is not None:
         a.inv_freq = inv_freq.data_ptr()
     if q is not None:
@@ -202,22 +201,27 @@ def rope_kv_append(q, q_out, k, v, k_cache4, v_cache4, block_ids, block_offsets,
         a.q_stride[:] = strides(q, 3)
         a.q_out = q_out.data_ptr()
         a.q_out_stride[:] = strides(q_out, 3)
-    a.k = k.data_ptr()
-    a.k_stride[:] = strides(k, 3)
-    a.v = v.data_ptr()
-    a.v_stride[:] = strides(v, 3)
-    a.k_cache = k_cache4.data_ptr()
-    a.k_cache_stride[:] = strides(k_cache4, 4)
-    a.v_cache = v_cache4.data_ptr()
-    a.v_cache_stride[:] = strides(v_cache4, 4)
-    a.block_ids = block_ids.data_ptr()
-    a.block_offsets = block_offsets.data_ptr()
-    a.block_ids_index = index_code(block_ids)
-    a.block_offsets_index = index_code(block_offsets)
+    if k is not None:
+        a.num_kv_heads = k.shape[1]
+        a.block_size = k_cache4.shape[2]
+        a.num_blocks = k_cache4.shape[0]
+        a.k = k.data_ptr()
+        a.k_stride[:] = strides(k, 3)
+        a.v = v.data_ptr()
+        a.v_stride[:] = strides(v, 3)
+        a.k_cache = k_cache4.data_ptr()
+        a.k_cache_stride[:] = strides(k_cache4, 4)
+        a.v_cache = v_cache4.data_ptr()
+        a.v_cache_stride[:] = strides(v_cache4, 4)
+        a.block_ids = block_ids.data_ptr()
+        a.block_offsets = block_offsets.data_ptr()
+        a.block_ids_index = index_code(block_ids)
+        a.block_offsets_index = index_code(block_offsets)
     if positions is not None:
         a.positions = positions.data_ptr()
         a.positions_index = index_code(positions)
-    _lib.check(lib.fd_rope_kv_append(ctypes.byref(a), ctypes.c_void_p(stream_handle(k.device))),
+    _lib.check(lib.fd_rope_kv_append(ctypes.byref(a),
+                                     ctypes.c_void_p(stream_handle(lead.device))),
                "fd_rope_kv_append")
 
 

@@ -113,16 +113,18 @@ extern "C" int fd_rope_kv_append(const fd_rope_kv_append_args* a, void* cuda_str
     return FD_ERR_INVALID_ARGUMENT;
   if (a->dtype != FD_DTYPE_F32 && a->dtype != FD_DTYPE_F16 && a->dtype != FD_DTYPE_BF16)
     return FD_ERR_UNSUPPORTED;
-  if (a->batch < 0 || a->num_kv_heads <= 0 || a->head_dim <= 0 || a->block_size <= 0 ||
-      a->num_blocks <= 0)
-    return FD_ERR_INVALID_ARGUMENT;
+  const bool has_q = a->q != nullptr;
+  const bool has_kv = a->num_kv_heads > 0;  // 0: rotate q only (no cache write)
+  if (a->batch < 0 || a->num_kv_heads < 0 || a->head_dim <= 0) return FD_ERR_INVALID_ARGUMENT;
+  if (!has_kv && !has_q) return FD_ERR_INVALID_ARGUMENT;
+  if (has_kv && (a->block_size <= 0 || a->num_blocks <= 0)) return FD_ERR_INVALID_ARGUMENT;
   if (a->rotary_dim < 0 || a->rotary_dim > a->head_dim || (a->rotary_dim & 1))
     return FD_ERR_INVALID_ARGUMENT;
   if (a->rotary_dim > 0 && !a->inv_freq) return FD_ERR_INVALID_ARGUMENT;
-  if (!a->k || !a->v || !a->k_cache || !a->v_cache || !a->block_ids || !a->block_offsets)
+  if (has_kv &&
+      (!a->k || !a->v || !a->k_cache || !a->v_cache || !a->block_ids || !a->block_offsets))
     return FD_ERR_INVALID_ARGUMENT;
-  if (a->rotary_dim > 0 && !a->positions) return FD_ERR_INVALID_ARGUMENT;
-  const bool has_q = a->q != nullptr;
+  if ((a->rotary_dim > 0 || has_q) && !a->positions) return FD_ERR_INVALID_ARGUMENT;
   if (has_q && (!a->q_out || a->num_q_heads <= 0)) return FD_ERR_INVALID_ARGUMENT;
   if (a->batch == 0) return FD_OK;
 

@@ -163,7 +163,11 @@ typedef struct fd_split_kv_reduce_args {
 
 int fd_split_kv_reduce(const fd_split_kv_reduce_args* args, void* cuda_stream);
 
-/* ---- fused RoPE + paged K/V append -------------------------------------- */
+/* ---- fused RoPE + paged K/V append --------------------------------------
+ * With num_kv_heads == 0 (and q given) the call only rotates q into q_out:
+ * k, v, the caches and the index pointers may then be NULL and positions is
+ * the only index read.  This is the native form of flashdec/rope.py:26-85
+ * (apply_rope) for device tensors. */
 typedef struct fd_rope_kv_append_args {
   int32_t struct_size;
   int32_t dtype;          /* FD_DTYPE_F32 / F16 / BF16 */
@@ -189,7 +193,7 @@ typedef struct fd_rope_kv_append_args {
   int64_t v_cache_stride[4];
   const void* block_ids;  /* [batch] */
   const void* block_offsets;
-  const void* positions;
+  const void* positions;  /* [batch]; required when q != NULL or rotary_dim > 0 */
   int32_t block_ids_index;
   int32_t block_offsets_index;
   int32_t positions_index;
