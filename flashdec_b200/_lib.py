@@ -19,6 +19,7 @@ FD_ERR_UNSUPPORTED = -2
 FD_ERR_WORKSPACE = -3
 FD_ERR_CUDA = -4
 FD_ERR_ALIGNMENT = -5
+FD_ERR_CAPACITY = -6
 FD_STATUS_WAIT_TIMEOUT = 1
 FD_STATUS_BAD_BLOCK_ID = 2
 
@@ -85,7 +86,7 @@ class RopeKVAppendArgs(ctypes.Structure):
 # Exported symbols declared in include/flashdec_b200.h
 EXPORTED_SYMBOLS = (
     "fd_paged_decode_workspace", "fd_paged_decode", "fd_split_kv_reduce", "fd_rope_kv_append",
-    "fd_error_string", "fd_version", "fd_device_status", "fd_num_sms",
+    "fd_error_string", "fd_version", "fd_device_status", "fd_num_sms", "fd_paged_decode_static",
 )
 
 _lock = threading.Lock()
@@ -118,6 +119,7 @@ def load_library():
         lib.fd_paged_decode_workspace.argtypes = [ctypes.POINTER(PagedDecodeArgs),
                                                   ctypes.POINTER(_sz), ctypes.POINTER(_i64)]
         lib.fd_paged_decode.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp]
+        lib.fd_paged_decode_static.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp]
         lib.fd_split_kv_reduce.argtypes = [ctypes.POINTER(SplitReduceArgs), _vp]
         lib.fd_rope_kv_append.argtypes = [ctypes.POINTER(RopeKVAppendArgs), _vp]
         lib.fd_error_string.argtypes = [ctypes.c_int]
@@ -125,7 +127,8 @@ def load_library():
         lib.fd_version.argtypes = []
         lib.fd_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         lib.fd_num_sms.argtypes = []
-        for name in ("fd_paged_decode_workspace", "fd_paged_decode", "fd_split_kv_reduce",
+        for name in ("fd_paged_decode_workspace", "fd_paged_decode", "fd_paged_decode_static",
+                     "fd_split_kv_reduce",
                      "fd_rope_kv_append", "fd_version", "fd_device_status", "fd_num_sms"):
             getattr(lib, name).restype = ctypes.c_int
         _lib = lib

@@ -211,6 +211,9 @@ const char* fd_error_string(int code) {
       return fd::g_last_cuda_error.empty() ? "CUDA error" : fd::g_last_cuda_error.c_str();
     case FD_ERR_ALIGNMENT:
       return "misaligned pointer or stride";
+    case FD_ERR_CAPACITY:
+      return "request needs more workspace than fd_paged_decode_static's static storage "
+             "(8 MiB scratch, 4096 tickets)";
     default:
       return "unknown error";
   }

@@ -45,6 +45,8 @@ extern "C" {
 #define FD_ERR_WORKSPACE (-3)         /* workspace missing or too small    */
 #define FD_ERR_CUDA (-4)              /* a CUDA runtime call failed        */
 #define FD_ERR_ALIGNMENT (-5)         /* pointer/stride alignment          */
+#define FD_ERR_CAPACITY (-6)          /* need exceeds fd_paged_decode_static's
+                                         static storage                    */
 
 /* device status word bits (fd_device_status) */
 #define FD_STATUS_WAIT_TIMEOUT 1      /* a bounded mbarrier wait ran out   */
@@ -137,6 +139,21 @@ int fd_paged_decode_workspace(const fd_paged_decode_args* args, size_t* scratch_
                               int64_t* tickets_needed);
 
 int fd_paged_decode(const fd_paged_decode_args* args, void* cuda_stream);
+
+/* fd_paged_decode with its ticket and scratch buffers taken from 8 MiB of
+ * fp32 scratch and 4096 int32 tickets that are static device storage of the
+ * library (the tickets/scratch fields of `args` are ignored), for callers
+ * that cannot allocate device memory.  No counterpart in the reference.
+ * - The first call on a device (that device current) looks up the storage
+ *   address; make it before any stream capture.
+ * - The tickets start at zero (zero-filled at module load) and every
+ *   completed call leaves them at zero; after a call that raised
+ *   FD_STATUS_WAIT_TIMEOUT, do not use this entry point again.
+ * - All calls on a device share the storage: calls that overlap on the GPU
+ *   race; order them (e.g. one stream).
+ * - A call needing more than the static storage (see
+ *   fd_paged_decode_workspace) returns FD_ERR_CAPACITY and launches nothing. */
+int fd_paged_decode_static(const fd_paged_decode_args* args, void* cuda_stream);
 
 /* ---- split-KV reducer --------------------------------------------------- */
 typedef struct fd_split_kv_reduce_args {

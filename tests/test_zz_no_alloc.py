@@ -1,0 +1,124 @@
+"""fd_paged_decode_static (the entry point that allocates nothing) against
+fd_paged_decode, both called through the C ABI.
+
+Two static calls in a row must agree with the regular entry point (same
+kernel, same plan) and with the numpy oracle; the second call also proves the
+static tickets were left at zero by the first.  This file is collected last
+and builds everything it needs itself, so it passes alone in a fresh process
+as well as after the other GPU tests."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle.paged_attention import paged_decode_attention_ref  # noqa: E402
+from tests.golden.cases import _normal  # noqa: E402
+from tests.helpers import assert_attention_close, to_dev, to_np  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _args(q, k4, v4, bt, sl, out, sm_scale, block_size):
+    from flashdec_b200 import _lib
+
+    a = _lib.PagedDecodeArgs()
+    a.struct_size = ctypes.sizeof(a)
+    a.dtype = _lib.FD_DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.FD_DTYPE_F16
+    a.num_seqs, a.num_q_heads, a.head_dim = q.shape
+    a.num_kv_heads = k4.shape[1]
+    a.block_size = block_size
+    a.num_blocks = k4.shape[0]
+    a.max_blocks_per_seq = bt.shape[1]
+    a.sm_scale = sm_scale
+    a.q, a.out = q.data_ptr(), out.data_ptr()
+    a.q_stride[:] = q.stride()
+    a.out_stride[:] = out.stride()
+    a.k_cache, a.v_cache = k4.data_ptr(), v4.data_ptr()
+    a.k_stride[:] = k4.stride()
+    a.v_stride[:] = v4.stride()
+    a.block_tables = bt.data_ptr()
+    a.block_tables_index = _lib.FD_INDEX_I32
+    a.block_tables_stride[:] = bt.stride()
+    a.seq_lens = sl.data_ptr()
+    a.seq_lens_index = _lib.FD_INDEX_I32
+    a.seq_lens_stride = sl.stride(0)
+    return a
+
+
+def _case(seed, lens, hq=16, hkv=2, d=128, bs=32):
+    rng = np.random.default_rng(seed)
+    nblk = [max(1, -(-n // bs)) for n in lens]
+    pool = 2 * sum(nblk)
+    q = _normal(rng, (len(lens), hq, d), "bfloat16")
+    k = _normal(rng, (pool, hkv, bs, d), "bfloat16")
+    v = _normal(rng, (pool, hkv, bs, d), "bfloat16")
+    perm = rng.permutation(pool)
+    bt = np.zeros((len(lens), max(nblk)), np.int32)
+    pos = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[pos:pos + n]
+        pos += n
+    return q, k, v, bt, np.asarray(lens, np.int32)
+
+
+@pytest.mark.parametrize("lens", [[2048] * 8, [1, 517, 4096, 33, 2000, 0, 129]])
+def test_static_entry_point_matches_regular_entry_point(lens):
+    from flashdec_b200 import _lib
+
+    lib = _lib.load_library()
+    q, k, v, bt, sl = _case(7, lens)
+    dq, dk, dv = to_dev(q, "bfloat16"), to_dev(k, "bfloat16"), to_dev(v, "bfloat16")
+    dbt, dsl = to_dev(bt), to_dev(sl)
+    scale = 128 ** -0.5
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    # regular entry point with a caller-owned, zero-filled workspace
+    ref_out = torch.empty_like(dq)
+    a = _args(dq, dk, dv, dbt, dsl, ref_out, scale, 32)
+    scratch_bytes, tickets_needed = ctypes.c_size_t(0), ctypes.c_int64(0)
+    _lib.check(lib.fd_paged_decode_workspace(ctypes.byref(a), ctypes.byref(scratch_bytes),
+                                             ctypes.byref(tickets_needed)), "workspace")
+    tickets = torch.zeros(max(1, tickets_needed.value), dtype=torch.int32, device="cuda")
+    scratch = torch.empty(max(1, (scratch_bytes.value + 3) // 4), dtype=torch.float32,
+                          device="cuda")
+    a.tickets, a.tickets_capacity = tickets.data_ptr(), tickets.numel()
+    a.scratch, a.scratch_bytes = scratch.data_ptr(), scratch.numel() * 4
+    _lib.check(lib.fd_paged_decode(ctypes.byref(a), stream), "fd_paged_decode")
+
+    outs = []
+    for _ in range(2):  # two calls in a row: the static tickets must be re-armed
+        out = torch.full_like(dq, float("nan"))
+        s = _args(dq, dk, dv, dbt, dsl, out, scale, 32)
+        _lib.check(lib.fd_paged_decode_static(ctypes.byref(s), stream), "static")
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+
+    want = paged_decode_attention_ref(q, k, v, bt, sl, sm_scale=scale)
+    for out in outs:
+        assert_attention_close(to_np(out), want)
+        assert torch.equal(out, ref_out)
+
+
+def test_static_entry_point_rejects_requests_beyond_its_storage():
+    from flashdec_b200 import _lib
+
+    lib = _lib.load_library()
+    # 4097 sequences x 8 KV heads need > 4096 tickets and > 8 MiB of slots
+    q = torch.zeros((4097, 8, 128), dtype=torch.bfloat16, device="cuda")
+    k4 = torch.zeros((1, 8, 16, 128), dtype=torch.bfloat16, device="cuda")
+    bt = torch.zeros((4097, 1), dtype=torch.int32, device="cuda")
+    sl = torch.ones(4097, dtype=torch.int32, device="cuda")
+    out = torch.full_like(q, 7.0)
+    a = _args(q, k4, k4, bt, sl, out, 1.0, 16)
+    rc = lib.fd_paged_decode_static(ctypes.byref(a),
+                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == _lib.FD_ERR_CAPACITY
+    assert b"static storage" in lib.fd_error_string(rc)
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())  # nothing was launched
