@@ -36,6 +36,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "fd_host.h"
 #include "fd_ptx.cuh"
@@ -48,7 +50,7 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kMaxRows = 16;  // query heads per head block (mma M)
 constexpr int kMaxStages = 16;
-constexpr int kMiscInts = 8;
+constexpr int kMiscInts = 16;  // [0] abort, [1] ticket winner, [8..9] cluster mbarrier
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kBarConsumers = 1;  // named barrier id for the consumer warps
@@ -84,6 +86,8 @@ struct AttnParams {
   int num_splits;  // 0 = length-balanced (stream-K) schedule
   int epilogue;    // FD_EPILOGUE_*
   int balanced;    // split mode: equal tile ranges instead of cdiv chunks
+  int cluster;     // split mode: the S CTAs of a pair form one thread-block
+                   // cluster and merge through distributed shared memory
   int cap_tiles;   // tiles of a full block-table row (speculative prefetch)
   int min_tiles_per_cta;
   // split-mode partials [seq, q_head, split, dim] / [seq, q_head, split]
@@ -310,6 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = tid & 31;
   volatile int* abort_flag = misc;
 
+  // cluster mode: arrivals of the S CTAs that push partials into this one
+  uint64_t* merge_bar = reinterpret_cast<uint64_t*>(misc + 8);
   if (tid < NST) {  // one stage's barriers per thread
     mbar_init(smem_u32(&full_bar[tid]), 1);
     mbar_init(smem_u32(&empty_bar[tid]), 1);
@@ -318,6 +324,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     misc[0] = 0;
     misc[1] = 0;
+    if (p.cluster) {
+      mbar_init(smem_u32(merge_bar), static_cast<uint32_t>(p.num_splits));
+      fence_mbar_init();
+    }
   }
   if (kTma && warp == kConsumerWarps && lane == 0) {
     prefetch_tensormap(&tmap_k);
@@ -396,6 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // one lane walking tile by tile.
   // =========================================================================
   if (warp == kConsumerWarps) {
+    // The producer touches no other CTA's memory; it arrives at the cluster
+    // barrier (paired with the consumers' wait before their first remote
+    // store) and may exit once its tiles are issued.
+    if (p.cluster) cluster_arrive();
     const uint64_t policy = l2_policy_evict_first();
     const int TG = max(1, min(32 >> ppt_shift, NST / 2));
     constexpr int kOps = 2 * SM::kHalves;  // boxes per page: K and V halves
@@ -597,6 +611,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // split schedule: the pair is known from blockIdx; load Q before the
     // sequence length arrives
     load_q(static_cast<int>(blockIdx.z), static_cast<int>(blockIdx.y));
+    // Cluster mode: obuf (which just held Q) becomes the receive buffer for
+    // the peers' partials.  This arrival, made after Q left obuf and after
+    // merge_bar was initialised, is what a peer waits for before its first
+    // store into this CTA.
+    if (p.cluster) cluster_arrive();
   }
 
   Segment s;
@@ -770,6 +789,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    // Cluster mode keeps obuf free for the peers' partials and merges in the
+    // stage ring instead, which is idle once every warp has consumed its
+    // last tile (one segment per CTA; the producer has nothing left to load).
+    float* wbuf = obuf;
+    if (p.cluster) {
+      named_barrier(kBarConsumers, kConsumerThreads);
+      wbuf = reinterpret_cast<float*>(stages);
+    }
     if (t4 == 0) {
       mlbuf[warp * kMaxRows + g8] = make_float2(m0, l0);
       mlbuf[warp * kMaxRows + g8 + 8] = make_float2(m1, l1);
@@ -777,13 +804,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) {
       const int d = 8 * j + 2 * t4;
-      *reinterpret_cast<float2*>(&obuf[(warp * kMaxRows + g8) * D + d]) =
+      *reinterpret_cast<float2*>(&wbuf[(warp * kMaxRows + g8) * D + d]) =
           make_float2(o[j][0], o[j][1]);
-      *reinterpret_cast<float2*>(&obuf[(warp * kMaxRows + g8 + 8) * D + d]) =
+      *reinterpret_cast<float2*>(&wbuf[(warp * kMaxRows + g8 + 8) * D + d]) =
           make_float2(o[j][2], o[j][3]);
     }
     named_barrier(kBarConsumers, kConsumerThreads);
     const int pid = s.b * p.nhb + s.hb;
+    // Cluster mode: row r of the pair is finished by CTA (r % S) of the
+    // cluster, which receives every CTA's (max, sum, acc) of that row in its
+    // obuf: acc at [(src * RI + r / S) * D + d], (max, sum) at
+    // mlr[src * RI + r / S].  Wait until every CTA of the cluster has made
+    // its obuf available (the arrival after Q staging).
+    const int csz = p.num_splits;
+    const int crank = p.cluster ? static_cast<int>(cluster_ctarank()) : 0;
+    const int cri = (nrows + csz - 1) / csz;  // rows finished per CTA (at most)
+    float2* mlr = reinterpret_cast<float2*>(obuf + csz * cri * D);
+    if (p.cluster) cluster_wait();
     for (int e = tid; e < nrows * (D / 4); e += kConsumerThreads) {
       const int r = e / (D / 4);
       const int d = (e - r * (D / 4)) * 4;
@@ -796,7 +833,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = 0; w < kConsumerWarps; ++w) {
           const float2 ml = mlbuf[w * kMaxRows + r];
           const float wgt = exp2f(ml.x - M);
-          const float4 ov = *reinterpret_cast<const float4*>(&obuf[(w * kMaxRows + r) * D + d]);
+          const float4 ov = *reinterpret_cast<const float4*>(&wbuf[(w * kMaxRows + r) * D + d]);
           L += wgt * ml.y;
           a0 += wgt * ov.x;
           a1 += wgt * ov.y;
@@ -804,7 +841,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           a3 += wgt * ov.w;
         }
       }
-      if (s.whole) {
+      if (p.cluster) {
+        // push this CTA's partial of row r to the row's owner (base-2 max)
+        const int owner = r % csz;
+        const int slot = crank * cri + r / csz;
+        st_cluster_v4(map_to_rank(smem_u32(&obuf[slot * D + d]), owner), a0, a1, a2, a3);
+        if (d == 0) st_cluster_v2(map_to_rank(smem_u32(&mlr[slot]), owner), M, L);
+      } else if (s.whole) {
         const float inv = L > 0.f ? 1.f / L : 0.f;
         store_out4<T>(p, s.b, head0 + r, d, a0 * inv, a1 * inv, a2 * inv, a3 * inv);
       } else {
@@ -824,7 +867,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (!s.whole && p.epilogue == FD_EPILOGUE_FUSED) {
+    if (p.cluster) {
+      // The named barrier orders every consumer thread's pushes before the
+      // release arrivals on the owners' merge barriers (one lane per owner);
+      // each owner waits for all S arrivals, which also tells it that no CTA
+      // will touch its shared memory again.
+      named_barrier(kBarConsumers, kConsumerThreads);
+      if (tid < csz) mbar_arrive_remote(map_to_rank(smem_u32(merge_bar), tid));
+      if (mbar_wait_cluster(smem_u32(merge_bar), 0u, p.status, abort_flag)) {
+        for (int e = tid; e < cri * (D / 4); e += kConsumerThreads) {
+          const int ri = e / (D / 4);
+          const int r = crank + ri * csz;
+          if (r >= nrows) continue;
+          const int d = (e - ri * (D / 4)) * 4;
+          float M = -INFINITY;
+          for (int src = 0; src < csz; ++src) M = fmaxf(M, mlr[src * cri + ri].x);
+          float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+          if (M != -INFINITY) {
+            for (int src = 0; src < csz; ++src) {
+              const float2 ml = mlr[src * cri + ri];
+              const float wgt = exp2f(ml.x - M);  // 0 for an empty split
+              const float4 ov =
+                  *reinterpret_cast<const float4*>(&obuf[(src * cri + ri) * D + d]);
+              L += wgt * ml.y;
+              a0 += wgt * ov.x;
+              a1 += wgt * ov.y;
+              a2 += wgt * ov.z;
+              a3 += wgt * ov.w;
+            }
+          }
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+          store_out4<T>(p, s.b, head0 + r, d, a0 * inv, a1 * inv, a2 * inv, a3 * inv);
+        }
+      }
+    } else if (!s.whole && p.epilogue == FD_EPILOGUE_FUSED) {
       // The barrier orders every consumer thread's partial stores before
       // thread 0's acq_rel ticket, which publishes them at GPU scope
       // (release) and, for the last arriver, makes the other CTAs' partials
@@ -1111,8 +1187,56 @@ WorkspaceNeed workspace_need(const fd_paged_decode_args& a, const Derived& dv, c
   return w;
 }
 
+// Clusters of the split schedule.  The S CTAs of a (sequence, head block)
+// pair can merge through distributed shared memory only if all clusters of
+// the launch are resident at once; cudaOccupancyMaxActiveClusters answers
+// that for this kernel, smem size and S (cached: the answer depends on the
+// device only).
+constexpr int kMaxClusterSize = 8;  // portable cluster size
+
+struct ClusterKey {
+  int device;
+  const void* kern;
+  size_t smem;
+  int size;
+};
+
+std::mutex g_cluster_mu;
+std::vector<std::pair<ClusterKey, int>> g_cluster_cache;
+
+template <typename K>
+int max_active_clusters(K kern, size_t smem, int size, const DeviceInfo& dev) {
+  {
+    std::lock_guard<std::mutex> lock(g_cluster_mu);
+    for (const auto& e : g_cluster_cache) {
+      if (e.first.device == dev.device && e.first.kern == reinterpret_cast<const void*>(kern) &&
+          e.first.smem == smem && e.first.size == size)
+        return e.second;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(size));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(size);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();  // not fatal: the launch falls back to the ticket merge
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(g_cluster_mu);
+  g_cluster_cache.push_back({ClusterKey{dev.device, reinterpret_cast<const void*>(kern), smem, size}, n});
+  return n;
+}
+
 template <typename T, int D, bool kTma>
-int launch(const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
+int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
            size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
   auto kern = paged_decode_kernel<T, D, kTma>;
   static std::once_flag once[64];
@@ -1123,16 +1247,42 @@ int launch(const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv, 
                                           dev.max_smem_optin);
   });
   if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
+  // Balanced split of a small batch: use the largest cluster size S <= the
+  // planned split count whose clusters all fit on the device at once.
+  int csize = 0;
+  if (prm.balanced && prm.num_splits >= 2 && prm.epilogue == FD_EPILOGUE_FUSED &&
+      cluster_enabled()) {
+    const int64_t clusters = static_cast<int64_t>(grid.y) * grid.z;
+    for (int sz = std::min(prm.num_splits, kMaxClusterSize); sz >= 2; --sz) {
+      if (max_active_clusters(kern, smem, sz, dev) >= clusters) {
+        csize = sz;
+        break;
+      }
+    }
+  }
+  if (csize >= 2) {
+    prm.num_splits = csize;
+    prm.cluster = 1;
+    grid.x = static_cast<unsigned>(csize);
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  int nattr = 1;
+  if (csize >= 2) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(csize);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    nattr = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm, mk, mv));
 }
 

@@ -113,6 +113,14 @@ bool pdl_enabled() {
   return on;
 }
 
+bool cluster_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLASHDEC_B200_CLUSTER");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return FD_OK;
   g_last_cuda_error = cudaGetErrorString(e);

@@ -51,6 +51,11 @@ int* device_status_ptr();
 // FLASHDEC_B200_PDL=0 turns it off).
 bool pdl_enabled();
 
+// Whether the small-batch split schedule may merge through thread-block
+// clusters (default on; FLASHDEC_B200_CLUSTER=0 turns it off and keeps the
+// global-memory ticket merge).
+bool cluster_enabled();
+
 // Launch `kern` with the programmatic-stream-serialization attribute (the
 // kernel calls griddepcontrol.wait before touching global memory).
 template <typename... KArgs, typename... Args>

@@ -1,8 +1,9 @@
 // Thin inline-PTX wrappers used by the FlashDec B200 kernels (sm_100a).
 //
-// Only documented PTX forms are used: mbarrier (shared::cta), the tiled TMA
-// load cp.async.bulk.tensor (no multicast), ldmatrix, mma.sync and proxy
-// fences.  Every mbarrier wait is bounded: a wait that runs out records
+// Only documented PTX forms are used: mbarrier (local, and arrive on a peer
+// CTA's barrier inside a cluster), the tiled TMA load cp.async.bulk.tensor
+// (no multicast), ldmatrix, mma.sync, proxy fences, the cluster barrier,
+// mapa and st.shared::cluster.  Every mbarrier wait is bounded: a wait that runs out records
 // FD_STATUS_WAIT_TIMEOUT in the device status word and reports failure so the
 // caller can wind the CTA down instead of spinning forever.
 #pragma once
@@ -215,6 +216,78 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
 
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---- thread-block clusters (distributed shared memory) -------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Hardware cluster barrier, split into its arrive (release) and wait
+// (acquire) halves.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Shared::cluster address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b)
+               : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster, releasing at cluster
+// scope every write that happens before it.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (arrivals come from other CTAs of
+// the cluster); same failure contract as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* status,
+                                                  volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 15u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(status, FD_STATUS_WAIT_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
 }
 
 }  // namespace fd
