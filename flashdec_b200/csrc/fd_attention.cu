@@ -55,6 +55,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kBarConsumers = 1;  // named barrier id for the consumer warps
 constexpr int kMergeBatch = 10;   // partials merged per register batch
+constexpr int kMaxClusterSize = 8;  // portable thread-block cluster size
 
 struct AttnParams {
   int num_seqs, num_q_heads, num_kv_heads, block_size, num_blocks, max_blocks;
@@ -113,6 +114,10 @@ struct Smem {
   static constexpr int kMergeFloats = kConsumerWarps * kMaxRows * D;
   static constexpr int kMergeBytes = kMergeFloats * 4 + kConsumerWarps * kMaxRows * 8;
 };
+
+// Column of element (row, col) in a merge buffer of 128-float-aligned rows:
+// XOR with 8 * (row % 4) so that consecutive rows start on different banks.
+__device__ __forceinline__ int merge_col(int row, int col) { return col ^ ((row & 3) << 3); }
 
 // Byte offset of element (row, dim) in a [32][D] tile stored as D/64 halves
 // of [32][64] with the TMA 128B swizzle (16-byte chunk index XOR row % 8).
@@ -801,12 +806,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mlbuf[warp * kMaxRows + g8] = make_float2(m0, l0);
       mlbuf[warp * kMaxRows + g8 + 8] = make_float2(m1, l1);
     }
+    // Rows of the merge buffer are 128-float aligned, so the eight rows one
+    // store instruction touches would share banks; the column is XORed with
+    // 8 * (row % 4) (merge_col), which keeps float2/float4 groups contiguous
+    // and spreads a store over all 32 banks.
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) {
       const int d = 8 * j + 2 * t4;
-      *reinterpret_cast<float2*>(&wbuf[(warp * kMaxRows + g8) * D + d]) =
+      const int r0 = warp * kMaxRows + g8;
+      *reinterpret_cast<float2*>(&wbuf[r0 * D + merge_col(r0, d)]) =
           make_float2(o[j][0], o[j][1]);
-      *reinterpret_cast<float2*>(&wbuf[(warp * kMaxRows + g8 + 8) * D + d]) =
+      *reinterpret_cast<float2*>(&wbuf[(r0 + 8) * D + merge_col(r0 + 8, d)]) =
           make_float2(o[j][2], o[j][3]);
     }
     named_barrier(kBarConsumers, kConsumerThreads);
@@ -833,7 +843,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = 0; w < kConsumerWarps; ++w) {
           const float2 ml = mlbuf[w * kMaxRows + r];
           const float wgt = exp2f(ml.x - M);
-          const float4 ov = *reinterpret_cast<const float4*>(&wbuf[(w * kMaxRows + r) * D + d]);
+          const int wr = w * kMaxRows + r;
+          const float4 ov = *reinterpret_cast<const float4*>(&wbuf[wr * D + merge_col(wr, d)]);
           L += wgt * ml.y;
           a0 += wgt * ov.x;
           a1 += wgt * ov.y;
@@ -880,20 +891,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r = crank + ri * csz;
           if (r >= nrows) continue;
           const int d = (e - ri * (D / 4)) * 4;
+          // all loads first (independent), then the merge
+          float2 ml[kMaxClusterSize];
+          float4 ov[kMaxClusterSize];
+#pragma unroll
+          for (int src = 0; src < kMaxClusterSize; ++src) {
+            ml[src] = make_float2(-INFINITY, 0.f);
+            ov[src] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (src < csz) {
+              ml[src] = mlr[src * cri + ri];
+              ov[src] = *reinterpret_cast<const float4*>(&obuf[(src * cri + ri) * D + d]);
+            }
+          }
           float M = -INFINITY;
-          for (int src = 0; src < csz; ++src) M = fmaxf(M, mlr[src * cri + ri].x);
+#pragma unroll
+          for (int src = 0; src < kMaxClusterSize; ++src) M = fmaxf(M, ml[src].x);
           float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
           if (M != -INFINITY) {
-            for (int src = 0; src < csz; ++src) {
-              const float2 ml = mlr[src * cri + ri];
-              const float wgt = exp2f(ml.x - M);  // 0 for an empty split
-              const float4 ov =
-                  *reinterpret_cast<const float4*>(&obuf[(src * cri + ri) * D + d]);
-              L += wgt * ml.y;
-              a0 += wgt * ov.x;
-              a1 += wgt * ov.y;
-              a2 += wgt * ov.z;
-              a3 += wgt * ov.w;
+#pragma unroll
+            for (int src = 0; src < kMaxClusterSize; ++src) {
+              const float wgt = exp2f(ml[src].x - M);  // 0 for an empty or absent split
+              L += wgt * ml[src].y;
+              a0 += wgt * ov[src].x;
+              a1 += wgt * ov[src].y;
+              a2 += wgt * ov[src].z;
+              a3 += wgt * ov[src].w;
             }
           }
           const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -1192,7 +1214,6 @@ WorkspaceNeed workspace_need(const fd_paged_decode_args& a, const Derived& dv, c
 // the launch are resident at once; cudaOccupancyMaxActiveClusters answers
 // that for this kernel, smem size and S (cached: the answer depends on the
 // device only).
-constexpr int kMaxClusterSize = 8;  // portable cluster size
 
 struct ClusterKey {
   int device;
