@@ -16,6 +16,7 @@ rebuilds those tensors on every layer write (cache.py:592, :1043-1076).
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass, replace
 from typing import Hashable
@@ -65,6 +66,128 @@ class _DeviceMeta:
         self.public = dict(positions=p64[:n], physical_block_ids=p64[n:2 * n],
                            block_offsets=p64[2 * n:3 * n], effective_seq_lens=p32[:n],
                            block_tables=p32[n:].view(n, width))
+
+
+class _FusedLayerLauncher:
+    """Launch state of the engine's fused layer step for one open token.
+
+    Both C-ABI argument structs (``fd_rope_kv_append`` and ``fd_paged_decode``)
+    are filled once per transaction from the cache-owned device metadata and
+    the per-device decode workspace; a layer then only sets its q/k/v/output
+    pointers and the layer's cache planes.  The arithmetic is the same as the
+    checked path (same kernels, same arguments), only the host marshalling is
+    done once instead of per layer.
+    """
+
+    def __init__(self, cache, meta, num_q_heads, sm_scale):
+        from . import _lib
+
+        self.lib = _lib.load_library()
+        self.check = _lib.check
+        n = meta.positions.numel()
+        hkv, d, bs = cache.num_kv_heads, cache.head_dim, cache.block_size
+        self.device = cache.device
+        self.qshape = (n, num_q_heads, d)
+        self.kvshape = (n, hkv, d)
+        kc, vc = cache.k_cache, cache.v_cache
+        esz = kc.element_size()
+        self.k_base, self.v_base = kc.data_ptr(), vc.data_ptr()
+        self.k_layer_bytes = kc.stride(0) * esz
+        self.v_layer_bytes = vc.stride(0) * esz
+        q_strides = (num_q_heads * d, d, 1)
+        kv_strides = (hkv * d, d, 1)
+
+        ra = _lib.RopeKVAppendArgs()
+        ra.struct_size = ctypes.sizeof(ra)
+        ra.dtype = _native.dtype_code(kc)
+        ra.batch = n
+        ra.num_q_heads = num_q_heads
+        ra.num_kv_heads = hkv
+        ra.head_dim = d
+        ra.block_size = bs
+        ra.num_blocks = cache.max_blocks
+        ra.q_stride[:] = q_strides
+        ra.q_out_stride[:] = q_strides
+        ra.k_stride[:] = kv_strides
+        ra.v_stride[:] = kv_strides
+        ra.k_cache_stride[:] = kc.stride()[1:]
+        ra.v_cache_stride[:] = vc.stride()[1:]
+        ra.block_ids = meta.block_ids.data_ptr()
+        ra.block_offsets = meta.offsets.data_ptr()
+        ra.positions = meta.positions.data_ptr()
+        ra.block_ids_index = ra.block_offsets_index = ra.positions_index = _lib.FD_INDEX_I64
+        self.ra = ra
+        self.rope_key = None
+
+        da = _lib.PagedDecodeArgs()
+        da.struct_size = ctypes.sizeof(da)
+        da.dtype = ra.dtype
+        da.num_seqs = n
+        da.num_q_heads = num_q_heads
+        da.num_kv_heads = hkv
+        da.head_dim = d
+        da.block_size = bs
+        da.num_blocks = cache.max_blocks
+        da.max_blocks_per_seq = meta.block_tables.shape[1]
+        da.sm_scale = float(sm_scale if sm_scale is not None else d ** -0.5)
+        da.q_stride[:] = q_strides
+        da.out_stride[:] = q_strides
+        da.k_stride[:] = kc.stride()[1:]
+        da.v_stride[:] = vc.stride()[1:]
+        da.block_tables = meta.block_tables.data_ptr()
+        da.block_tables_index = _lib.FD_INDEX_I32
+        da.block_tables_stride[:] = meta.block_tables.stride()
+        da.seq_lens = meta.eff_seq_lens.data_ptr()
+        da.seq_lens_index = _lib.FD_INDEX_I32
+        da.seq_lens_stride = 1
+        da.epilogue = _lib.FD_EPILOGUE_FUSED
+        # the plan (and so the workspace need) depends on shapes only
+        da.q = da.out = da.k_cache = da.v_cache = 1
+        scratch = ctypes.c_size_t(0)
+        tickets = ctypes.c_int64(0)
+        self.check(self.lib.fd_paged_decode_workspace(ctypes.byref(da), ctypes.byref(scratch),
+                                                      ctypes.byref(tickets)),
+                   "fd_paged_decode_workspace")
+        self.workspace = (None, None)
+        if scratch.value or tickets.value:
+            # held here so that a later growth of the shared per-device
+            # workspace cannot free the buffers this transaction points at
+            t, s = self.workspace = _native.workspace(self.device, tickets.value, scratch.value)
+            if t is not None:
+                da.tickets, da.tickets_capacity = t.data_ptr(), t.numel()
+            if s is not None:
+                da.scratch, da.scratch_bytes = s.data_ptr(), s.numel() * 4
+        self.da = da
+
+    def _set_rope(self, rotary_dim, base):
+        key = (rotary_dim, base)
+        if key != self.rope_key:
+            self.ra.rotary_dim = rotary_dim
+            self.ra.inv_freq = _native.inv_freq_device(rotary_dim, base, self.device).data_ptr()
+            self.rope_key = key
+
+    def run(self, layer_idx, q, k, v, rotary_dim, base):
+        """RoPE + K/V store, then decode; returns ``(q_rotated, output)``."""
+        if tuple(q.shape) != self.qshape or not q.is_contiguous():
+            raise ValueError("q must be a contiguous [num_requests, num_q_heads, head_dim] tensor "
+                             "matching the transaction")
+        if tuple(k.shape) != self.kvshape or tuple(v.shape) != self.kvshape or \
+                not k.is_contiguous() or not v.is_contiguous():
+            raise ValueError("k and v must be contiguous [num_requests, num_kv_heads, head_dim] "
+                             "tensors matching the transaction")
+        self._set_rope(rotary_dim, base)
+        q_rot = torch.empty_like(q)
+        out = torch.empty_like(q)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        ra, da = self.ra, self.da
+        kc = self.k_base + layer_idx * self.k_layer_bytes
+        vc = self.v_base + layer_idx * self.v_layer_bytes
+        ra.q, ra.q_out, ra.k, ra.v = q.data_ptr(), q_rot.data_ptr(), k.data_ptr(), v.data_ptr()
+        ra.k_cache, ra.v_cache = kc, vc
+        self.check(self.lib.fd_rope_kv_append(ctypes.byref(ra), stream), "fd_rope_kv_append")
+        da.q, da.out, da.k_cache, da.v_cache = q_rot.data_ptr(), out.data_ptr(), kc, vc
+        self.check(self.lib.fd_paged_decode(ctypes.byref(da), stream), "fd_paged_decode")
+        return q_rot, out
 
 
 class PagedKVCache:
@@ -286,6 +409,42 @@ class PagedKVCache:
                                              self.v_cache[layer_idx], meta.block_ids,
                                              meta.offsets, meta.positions, rotary_dim=rotary_dim,
                                              base=base, q_out=q_out)
+
+    def _fused_layer_step(self, transaction, layer_idx, q, k, v, rotary_dim, base, sm_scale):
+        """Engine fast path of one layer: fused RoPE + K/V store at the
+        reserved slots, then paged decode over the transaction's block tables
+        and effective lengths.  Returns ``(q_rotated, output, public
+        metadata)``; the launch arguments are prepared once per transaction
+        (:class:`_FusedLayerLauncher`)."""
+        state = self._require_open_transaction(transaction)
+        try:
+            layer_idx = self._ledger.check_layer_for_write(state, layer_idx)
+            self._require_cuda("write_token_layer_fused_cuda")
+            if not all(isinstance(t, torch.Tensor) for t in (q, k, v)):
+                raise TypeError("q, k, and v must be torch tensors")
+            if q.device != self.device or k.device != self.device or v.device != self.device:
+                raise ValueError("q, k, and v must be on the cache device")
+            if q.dtype != self.dtype or k.dtype != self.dtype or v.dtype != self.dtype:
+                raise ValueError("q, k, and v must use the cache dtype")
+            if q.dim() != 3 or q.shape[1] <= 0:
+                raise ValueError("q shape must match transaction request count and cache head_dim")
+            rotary_dim = self._check_rope_args(rotary_dim, base)
+            meta = state.device_view
+            key = (int(q.shape[1]), sm_scale)
+            launcher = getattr(meta, "launcher", None)
+            if launcher is None or meta.launcher_key != key:
+                launcher = _FusedLayerLauncher(self, meta, key[0], sm_scale)
+                meta.launcher, meta.launcher_key = launcher, key
+            if torch.cuda.current_device() != self.device.index:
+                with torch.cuda.device(self.device):
+                    q_rot, out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
+            else:
+                q_rot, out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
+        except Exception:
+            self._ledger.transaction_failure_count += 1
+            raise
+        self._ledger.record_layer_write(state, layer_idx)
+        return q_rot, out, meta.public
 
     def commit_token(self, transaction):
         """Publish one token after every layer has been written."""

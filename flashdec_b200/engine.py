@@ -290,6 +290,19 @@ class DecodeEngine:
                 k = k.unsqueeze(0)
             if v.dim() == 2:
                 v = v.unsqueeze(0)
+            if self.append_backend == "fused_cuda" and self._range is None:
+                # one prepared launch pair per layer (same kernels and
+                # arguments as the checked path below)
+                _, out, pub = self.cache._fused_layer_step(st.cache_tx, layer_idx, q, k, v,
+                                                           rotary_dim, base, self.sm_scale)
+                st.next_layer_idx += 1
+                st.last_output = out
+                self._transaction_layer_step_count += 1
+                return DecodeLayerResult(
+                    transaction_id=st.handle.transaction_id, layer_idx=layer_idx,
+                    request_ids=st.handle.request_ids, output=out,
+                    positions=pub["positions"], block_tables=pub["block_tables"],
+                    effective_seq_lens=pub["effective_seq_lens"])
             if self._range is None:
                 q_rot, view = self._write_layer(st, layer_idx, q, k, v, rotary_dim, base)
                 out = self._decode(q_rot, view.block_tables, view.effective_seq_lens, layer_idx)
