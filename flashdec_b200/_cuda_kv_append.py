@@ -60,11 +60,10 @@ def _validate_inputs(k_cache, v_cache, block_ids, block_offsets, k, v):
         raise ValueError("K/V caches and values must share one dtype")
     if str(k_cache.dtype).removeprefix("torch.") not in _SUPPORTED_DTYPES:
         raise ValueError("CUDA KV append supports float16, bfloat16, and float32")
-    if bool(torch.any(block_ids < 0).item()) or bool(torch.any(block_ids >= k_cache.shape[0]).item()):
+    rb, ro = _native.index_ranges(block_ids, block_offsets)  # one synchronisation
+    if rb is not None and (rb[0] < 0 or rb[1] >= k_cache.shape[0]):
         raise ValueError("block_ids must be within [0, num_blocks)")
-    if bool(torch.any(block_offsets < 0).item()) or bool(
-        torch.any(block_offsets >= k_cache.shape[2]).item()
-    ):
+    if ro is not None and (ro[0] < 0 or ro[1] >= k_cache.shape[2]):
         raise ValueError("block_offsets must be within [0, block_size)")
 
 

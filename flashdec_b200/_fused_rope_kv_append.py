@@ -89,14 +89,14 @@ def _validate_structure(q, k, v, k_cache, v_cache, block_ids, block_offsets, pos
 
 
 def _validate_index_values(block_ids, block_offsets, positions, num_blocks, block_size):
-    """Synchronous value checks of caller-owned indices (reference :128-146)."""
-    if bool(torch.any(block_ids < 0).item()) or bool(torch.any(block_ids >= num_blocks).item()):
+    """Value checks of caller-owned indices (reference :128-146): the same
+    checks in the same order, evaluated with one host synchronisation."""
+    rb, ro, rp = _native.index_ranges(block_ids, block_offsets, positions)
+    if rb is not None and (rb[0] < 0 or rb[1] >= num_blocks):
         raise ValueError("block_ids must be within [0, num_blocks)")
-    if bool(torch.any(block_offsets < 0).item()) or bool(
-        torch.any(block_offsets >= block_size).item()
-    ):
+    if ro is not None and (ro[0] < 0 or ro[1] >= block_size):
         raise ValueError("block_offsets must be within [0, block_size)")
-    if bool(torch.any(positions < 0).item()):
+    if rp is not None and rp[0] < 0:
         raise ValueError("positions must be non-negative")
 
 

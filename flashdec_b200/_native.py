@@ -38,6 +38,22 @@ def strides(t: torch.Tensor, n: int):
     return s
 
 
+def index_ranges(*tensors):
+    """``[(min, max), ...]`` of integer device tensors with one host
+    synchronisation (one aminmax per tensor, one device-to-host read); an
+    empty tensor gives ``None``."""
+    parts, where = [], []
+    for t in tensors:
+        if t.numel() == 0:
+            where.append(None)
+            continue
+        lo, hi = torch.aminmax(t)
+        where.append(len(parts))
+        parts += [lo.to(torch.int64), hi.to(torch.int64)]
+    vals = torch.stack(parts).tolist() if parts else []
+    return [None if w is None else (vals[w], vals[w + 1]) for w in where]
+
+
 # --------------------------------------------------------------------------
 # workspace: a zero-filled int32 ticket array (the kernel leaves it zero) and
 # fp32 scratch, per device, grown on demand and reused by every call on that

@@ -126,3 +126,15 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setenv("FLASHDEC_B200_LIB", str(tmp_path / "absent.so"))
     with pytest.raises(RuntimeError, match="no fallback"):
         _lib.load_library()
+
+
+def test_index_ranges_reads_all_ranges_in_one_pass():
+    import torch
+
+    from flashdec_b200 import _native
+
+    a = torch.tensor([3, -1, 7])
+    b = torch.tensor([], dtype=torch.int64)
+    c = torch.tensor([5], dtype=torch.int32)
+    assert _native.index_ranges(a, b, c) == [(-1, 7), None, (5, 5)]
+    assert _native.index_ranges() == []
