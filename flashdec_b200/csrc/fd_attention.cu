@@ -282,6 +282,13 @@ template <typename T>
 __device__ __forceinline__ void store_out4(const AttnParams& p, int b, int h, int d, float a0,
                                            float a1, float a2, float a3) {
   T* o = static_cast<T*>(p.out) + b * p.os0 + h * p.os1 + d * p.os2;
+  if (p.os2 == 1 && (reinterpret_cast<uintptr_t>(o) & 7u) == 0) {
+    uint2 v;
+    v.x = pack2<T>(a0, a1);
+    v.y = pack2<T>(a2, a3);
+    *reinterpret_cast<uint2*>(o) = v;
+    return;
+  }
   o[0] = from_f32<T>(a0);
   o[p.os2] = from_f32<T>(a1);
   o[2 * p.os2] = from_f32<T>(a2);
@@ -619,8 +626,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Cluster mode: obuf (which just held Q) becomes the receive buffer for
     // the peers' partials.  This arrival, made after Q left obuf and after
     // merge_bar was initialised, is what a peer waits for before its first
-    // store into this CTA.
-    if (p.cluster) cluster_arrive();
+    // store into this CTA.  The wait follows at once: the peers reach this
+    // point at about the same time, and the consumers would otherwise only
+    // wait for their first tile here.
+    if (p.cluster) {
+      cluster_arrive();
+      cluster_wait();
+    }
   }
 
   Segment s;
@@ -830,7 +842,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int crank = p.cluster ? static_cast<int>(cluster_ctarank()) : 0;
     const int cri = (nrows + csz - 1) / csz;  // rows finished per CTA (at most)
     float2* mlr = reinterpret_cast<float2*>(obuf + csz * cri * D);
-    if (p.cluster) cluster_wait();
     for (int e = tid; e < nrows * (D / 4); e += kConsumerThreads) {
       const int r = e / (D / 4);
       const int d = (e - r * (D / 4)) * 4;
