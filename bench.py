@@ -362,14 +362,14 @@ def run_ours(args, rank, world, local_rank):
     }
 
 
-def run_ragged(torch, dist, device, rank, world, stream, args):
+def run_ragged(torch, dist, device, rank, world, stream, args, batch=64):
     """B=64 Llama-3-8B attention shape (32q/8kv, D128,
     bs16) with log-uniform lengths in [512, 131072], LPT-sharded."""
     import flashdec_b200
     from flashdec_b200.sharding import lpt_partition
     from oracle.paged_attention import attention_bytes
 
-    lens = ragged_requests()
+    lens = ragged_requests(batch=batch)
     shards = lpt_partition(lens, world)
     mine = [lens[i] for i in shards[rank]]
     hq, hkv, d, bs = 32, 8, 128, 16
@@ -482,7 +482,7 @@ def run_c2_ctx1024(torch, device, stream, args):
             "algorithmic_bytes": nbytes, "hbm_gbs": gbs, "frac_of_peak": gbs / peak}
 
 
-def run_c3(torch, device, stream):
+def run_c3(torch, device, stream, cpu_seconds=2.0, api_reps=200):
     """fused RoPE + KV append of 64 tokens (16 q heads,
     2 KV heads, D128, theta 1e6) into distinct slots of a 4096 x 32 pool."""
     import numpy as np
@@ -510,12 +510,11 @@ def run_c3(torch, device, stream):
     us = _graph_time_us(torch, stream, step, reps=200, inner=50)
     # end to end through the public API (value checks synchronise, as in the reference)
     e0 = time.perf_counter()
-    reps = 200
-    for _ in range(reps):
+    for _ in range(api_reps):
         flashdec_b200.fused_rope_kv_append(q, k, v, kc, vc, bid, off, pos, rotary_dim=d,
                                            base=1e6)
     torch.cuda.synchronize()
-    api_us = (time.perf_counter() - e0) * 1e6 / reps
+    api_us = (time.perf_counter() - e0) * 1e6 / api_reps if api_reps else None
     nbytes = 2 * n * hq * d * 2 + 2 * n * hkv * d * 2 + 2 * n * hkv * d * 2 + 3 * n * 8
     # CPU reference on the same inputs: the oracle's RoPE of Q and K (a
     # restatement of flashdec/rope.py:26-85) and in-place slot writes
@@ -527,13 +526,13 @@ def run_c3(torch, device, stream):
     bh, oh, ph = bid.cpu().numpy(), off.cpu().numpy(), pos.cpu().numpy()
     t0 = time.perf_counter()
     cpu_reps = 0
-    while time.perf_counter() - t0 < 2.0:
+    while time.perf_counter() - t0 < cpu_seconds:
         apply_rope_ref(qh, ph, d, 1e6, "bfloat16")
         k_rot = apply_rope_ref(kh, ph, d, 1e6, "bfloat16")
         kch[bh, :, oh, :] = k_rot
         vch[bh, :, oh, :] = vh
         cpu_reps += 1
-    cpu_us = (time.perf_counter() - t0) * 1e6 / cpu_reps
+    cpu_us = (time.perf_counter() - t0) * 1e6 / cpu_reps if cpu_reps else None
     return {"workload": "BASELINE c3: fused RoPE + KV append, 64 tokens, 16q/2kv, D128, "
                         "theta 1e6, distinct slots in a 4096x32 pool",
             "us_per_call_device": us, "us_per_call_public_api": api_us,
@@ -722,9 +721,11 @@ def main():
     ap.add_argument("--steps", type=int, default=120000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--kernel-only", action="store_true",
-                    help="time only the device-resident c2 step (no e2e, ragged or CPU "
-                         "legs); the small case used for ncu captures")
+    ap.add_argument("--kernel-only", nargs="?", const="c2", default=None,
+                    choices=["c2", "c3", "c4"],
+                    help="time only one device-resident workload (no e2e or CPU legs): c2 "
+                         "(default), c3 (fused RoPE + append) or c4 (16 requests of the ragged "
+                         "batch, 1.5 GB of KV); the small cases used for ncu captures")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -734,6 +735,18 @@ def main():
         res = run_reference(args, rank, world)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.kernel_only in ("c3", "c4"):
+        import torch
+
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        stream = torch.cuda.Stream(device)
+        if args.kernel_only == "c3":
+            res = run_c3(torch, device, stream, cpu_seconds=0.0, api_reps=0)
+        else:
+            res = run_ragged(torch, None, device, 0, 1, stream, args, batch=16)
+        print(json.dumps({"kernel_only": args.kernel_only, **res}), flush=True)
         return
     import torch
     import torch.distributed as dist
