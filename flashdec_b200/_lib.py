@@ -87,6 +87,7 @@ class RopeKVAppendArgs(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "fd_paged_decode_workspace", "fd_paged_decode", "fd_split_kv_reduce", "fd_rope_kv_append",
     "fd_error_string", "fd_version", "fd_device_status", "fd_num_sms", "fd_paged_decode_static",
+    "fd_selftest_wait_timeout",
 )
 
 _lock = threading.Lock()
@@ -127,8 +128,9 @@ def load_library():
         lib.fd_version.argtypes = []
         lib.fd_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         lib.fd_num_sms.argtypes = []
+        lib.fd_selftest_wait_timeout.argtypes = [ctypes.c_int64, _vp]
         for name in ("fd_paged_decode_workspace", "fd_paged_decode", "fd_paged_decode_static",
-                     "fd_split_kv_reduce",
+                     "fd_split_kv_reduce", "fd_selftest_wait_timeout",
                      "fd_rope_kv_append", "fd_version", "fd_device_status", "fd_num_sms"):
             getattr(lib, name).restype = ctypes.c_int
         _lib = lib

@@ -70,14 +70,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // kWaitLimitNs (recording FD_STATUS_WAIT_TIMEOUT and raising the CTA's
 // abort flag) or if another warp of the CTA already raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 15u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         atomicOr(status, FD_STATUS_WAIT_TIMEOUT);
         *abort_flag = 1;
         return false;

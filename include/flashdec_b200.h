@@ -155,6 +155,13 @@ int fd_paged_decode(const fd_paged_decode_args* args, void* cuda_stream);
  *   fd_paged_decode_workspace) returns FD_ERR_CAPACITY and launches nothing. */
 int fd_paged_decode_static(const fd_paged_decode_args* args, void* cuda_stream);
 
+/* Diagnostic: launch one warp that waits, through the kernels' bounded
+ * mbarrier wait, on a barrier nothing arrives on, for `limit_ns` (1 ns .. 5 s).
+ * It then raises FD_STATUS_WAIT_TIMEOUT in the device status word and returns;
+ * the context stays usable.  Used to test the failure path without a GPU
+ * fault.  No counterpart in the reference. */
+int fd_selftest_wait_timeout(int64_t limit_ns, void* cuda_stream);
+
 /* ---- split-KV reducer --------------------------------------------------- */
 typedef struct fd_split_kv_reduce_args {
   int32_t struct_size;

@@ -119,6 +119,7 @@ def test_host_argument_checks_answer_without_a_gpu(lib):
     s = _lib.SplitReduceArgs()
     s.struct_size = 4
     assert lib.fd_split_kv_reduce(ctypes.byref(s), None) == _lib.FD_ERR_INVALID_ARGUMENT
+    assert lib.fd_selftest_wait_timeout(0, None) == _lib.FD_ERR_INVALID_ARGUMENT
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
