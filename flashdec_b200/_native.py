@@ -27,7 +27,16 @@ def index_code(t: torch.Tensor) -> int:
     return _INDEX_CODE[t.dtype]
 
 
+try:  # raw handle of the current stream without building a torch Stream object
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
 def stream_handle(device) -> int:
+    if _raw_stream is not None:
+        index = device.index if isinstance(device, torch.device) else device
+        return _raw_stream(torch.cuda.current_device() if index is None else index)
     return torch.cuda.current_stream(device).cuda_stream
 
 

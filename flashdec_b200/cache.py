@@ -118,6 +118,8 @@ class _FusedLayerLauncher:
         ra.block_ids_index = ra.block_offsets_index = ra.positions_index = _lib.FD_INDEX_I64
         self.ra = ra
         self.rope_key = None
+        self.rope_args = None  # last (rotary_dim, base) as given, and its checked form
+        self.rope_checked = None
 
         da = _lib.PagedDecodeArgs()
         da.struct_size = ctypes.sizeof(da)
@@ -176,9 +178,10 @@ class _FusedLayerLauncher:
             raise ValueError("k and v must be contiguous [num_requests, num_kv_heads, head_dim] "
                              "tensors matching the transaction")
         self._set_rope(rotary_dim, base)
-        q_rot = torch.empty_like(q)
-        out = torch.empty_like(q)
-        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        # rotated q and output share one allocation (two contiguous halves)
+        buf = torch.empty((2,) + self.qshape, dtype=q.dtype, device=q.device)
+        q_rot, out = buf[0], buf[1]
+        stream = ctypes.c_void_p(_native.stream_handle(self.device))
         ra, da = self.ra, self.da
         kc = self.k_base + layer_idx * self.k_layer_bytes
         vc = self.v_base + layer_idx * self.v_layer_bytes
@@ -416,25 +419,23 @@ class PagedKVCache:
         and effective lengths.  Returns ``(q_rotated, output, public
         metadata)``; the launch arguments are prepared once per transaction
         (:class:`_FusedLayerLauncher`)."""
+        # The engine has already checked q/k/v (tensors, shapes, device,
+        # dtype); this adds the transaction, layer order, contiguity (in
+        # run) and RoPE argument checks.
         state = self._require_open_transaction(transaction)
         try:
             layer_idx = self._ledger.check_layer_for_write(state, layer_idx)
-            self._require_cuda("write_token_layer_fused_cuda")
-            if not all(isinstance(t, torch.Tensor) for t in (q, k, v)):
-                raise TypeError("q, k, and v must be torch tensors")
-            if q.device != self.device or k.device != self.device or v.device != self.device:
-                raise ValueError("q, k, and v must be on the cache device")
-            if q.dtype != self.dtype or k.dtype != self.dtype or v.dtype != self.dtype:
-                raise ValueError("q, k, and v must use the cache dtype")
-            if q.dim() != 3 or q.shape[1] <= 0:
-                raise ValueError("q shape must match transaction request count and cache head_dim")
-            rotary_dim = self._check_rope_args(rotary_dim, base)
             meta = state.device_view
             key = (int(q.shape[1]), sm_scale)
             launcher = getattr(meta, "launcher", None)
             if launcher is None or meta.launcher_key != key:
+                self._require_cuda("write_token_layer_fused_cuda")
                 launcher = _FusedLayerLauncher(self, meta, key[0], sm_scale)
                 meta.launcher, meta.launcher_key = launcher, key
+            if (rotary_dim, base) != launcher.rope_args:
+                launcher.rope_checked = self._check_rope_args(rotary_dim, base)
+                launcher.rope_args = (rotary_dim, base)
+            rotary_dim = launcher.rope_checked
             if torch.cuda.current_device() != self.device.index:
                 with torch.cuda.device(self.device):
                     q_rot, out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
