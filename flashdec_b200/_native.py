@@ -106,10 +106,37 @@ def reserve_workspace(device, tickets: int, scratch_bytes: int) -> None:
 # --------------------------------------------------------------------------
 # paged decode
 # --------------------------------------------------------------------------
-def paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, block_size, num_seqs,
-                 num_splits=0, epilogue=_lib.FD_EPILOGUE_FUSED, append_k=None, append_v=None,
-                 slot_mapping=None, partials=None, max_ctas=0, min_tiles_per_cta=0):
-    """Launch fd_paged_decode.
+class PreparedDecode:
+    """``fd_paged_decode`` arguments prepared once for one call signature
+    (shapes, strides, dtypes, scalars) together with the workspace they
+    point at; :meth:`launch` only sets the data pointers.  A lock keeps two
+    threads from interleaving on the shared struct (ctypes releases the GIL
+    during the foreign call)."""
+
+    __slots__ = ("lib", "args", "workspace", "lock")
+
+    def __init__(self, lib, args, workspace):
+        self.lib = lib
+        self.args = args
+        self.workspace = workspace  # held: a later workspace growth cannot free it
+        self.lock = threading.Lock()
+
+    def launch(self, q, k, v, block_tables, seq_lens, out, stream):
+        a = self.args
+        with self.lock:
+            a.q, a.out = q.data_ptr(), out.data_ptr()
+            a.k_cache, a.v_cache = k.data_ptr(), v.data_ptr()
+            a.block_tables, a.seq_lens = block_tables.data_ptr(), seq_lens.data_ptr()
+            rc = self.lib.fd_paged_decode(ctypes.byref(a), ctypes.c_void_p(stream))
+        _lib.check(rc, "fd_paged_decode")
+
+
+def prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, block_size,
+                         num_seqs, num_splits=0, epilogue=_lib.FD_EPILOGUE_FUSED, append_k=None,
+                         append_v=None, slot_mapping=None, partials=None, max_ctas=0,
+                         min_tiles_per_cta=0):
+    """Fill the ``fd_paged_decode`` struct for these tensors and size the
+    workspace; returns a :class:`PreparedDecode`.
 
     ``k4``/``v4`` are 4-D views in logical order [block, kv_head, token, dim]
     (any strides).  ``partials`` = (acc, max, sum) in the reference split
@@ -165,15 +192,25 @@ def paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, block_size
     _lib.check(lib.fd_paged_decode_workspace(ctypes.byref(a), ctypes.byref(scratch_bytes),
                                              ctypes.byref(tickets_needed)),
                "fd_paged_decode_workspace")
+    ws = (None, None)
     if scratch_bytes.value or tickets_needed.value:
-        tickets, scratch = workspace(q.device, tickets_needed.value, scratch_bytes.value)
+        ws = tickets, scratch = workspace(q.device, tickets_needed.value, scratch_bytes.value)
         if tickets is not None:
             a.tickets = tickets.data_ptr()
             a.tickets_capacity = tickets.numel()
         if scratch is not None:
             a.scratch = scratch.data_ptr()
             a.scratch_bytes = scratch.numel() * 4
-    _lib.check(lib.fd_paged_decode(ctypes.byref(a), ctypes.c_void_p(stream_handle(q.device))),
+    return PreparedDecode(lib, a, ws)
+
+
+def paged_decode(q, k4, v4, block_tables, seq_lens, out, **kw):
+    """Prepare and launch ``fd_paged_decode`` on the current stream; returns
+    ``out``.  Keyword arguments as :func:`prepare_paged_decode`."""
+    prep = prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, **kw)
+    a = prep.args
+    _lib.check(prep.lib.fd_paged_decode(ctypes.byref(a),
+                                        ctypes.c_void_p(stream_handle(q.device))),
                "fd_paged_decode")
     return out
 

@@ -34,6 +34,36 @@ _KV_LAYOUT_AXES = {
 }
 
 
+# Prepared launches of the common call (no split workspace, no fused append),
+# keyed by everything the checks and the launch arguments depend on: shapes,
+# strides, dtypes and devices of every tensor plus the scalar arguments.  A
+# signature that passed the full checks once passes them again, so a hit only
+# sets the data pointers and launches.
+_PREPARED: dict = {}
+_PREPARED_LIMIT = 256
+
+
+def _signature(q, k_cache, v_cache, block_tables, seq_lens, out, sm_scale, block_size, num_warps,
+               kv_layout, num_stages):
+    return (q.shape, q.stride(), q.dtype, q.device,
+            k_cache.shape, k_cache.stride(), k_cache.dtype, k_cache.device,
+            v_cache.shape, v_cache.stride(), v_cache.dtype, v_cache.device,
+            block_tables.shape, block_tables.stride(), block_tables.dtype, block_tables.device,
+            seq_lens.shape, seq_lens.stride(), seq_lens.dtype, seq_lens.device,
+            out.shape, out.stride(), out.dtype, out.device,
+            sm_scale, block_size, num_warps, kv_layout, num_stages)
+
+
+def _launch_prepared(prep, q, k_cache, v_cache, block_tables, seq_lens, out):
+    dev = q.device
+    if torch.cuda.current_device() == dev.index:
+        prep.launch(q, k_cache, v_cache, block_tables, seq_lens, out, _native.stream_handle(dev))
+    else:
+        with torch.cuda.device(dev):
+            prep.launch(q, k_cache, v_cache, block_tables, seq_lens, out,
+                        _native.stream_handle(dev))
+
+
 def _layout_axes(kv_layout):
     try:
         return _KV_LAYOUT_AXES[kv_layout]
@@ -190,6 +220,21 @@ def paged_decode_attention_into(
     attention launch; rows with ``slot_mapping < 0`` get a zero output and no
     store.
     """
+    key = None
+    if (split_kv_workspace is None and type(num_splits) is int and num_splits == 1
+            and append_k is None and append_v is None and slot_mapping is None):
+        try:
+            key = _signature(q, k_cache, v_cache, block_tables, seq_lens, out, sm_scale,
+                             block_size, num_warps, kv_layout, num_stages)
+            hash(key)
+        except (AttributeError, TypeError):
+            key = None
+        if key is not None:
+            prep = _PREPARED.get(key)
+            if prep is not None:
+                _launch_prepared(prep, q, k_cache, v_cache, block_tables, seq_lens, out)
+                return out
+
     token_axis, _ = _layout_axes(kv_layout)
     if block_size is None:
         if k_cache.dim() != 4:
@@ -272,6 +317,16 @@ def paged_decode_attention_into(
             )
             _native.split_kv_reduce(acc, mx, sm, seq_lens, out, num_seqs=num_seqs,
                                     slot_mapping=slot_mapping if fuse_kv_append else None)
+            return out
+        if key is not None:
+            prep = _native.prepare_paged_decode(
+                q, k4, v4, block_tables, seq_lens, out, sm_scale=sm_scale,
+                block_size=block_size, num_seqs=num_seqs, num_splits=0)
+            if len(_PREPARED) >= _PREPARED_LIMIT:
+                _PREPARED.clear()
+            _PREPARED[key] = prep
+            prep.launch(q, k_cache, v_cache, block_tables, seq_lens, out,
+                        _native.stream_handle(q.device))
             return out
         _native.paged_decode(
             q, k4, v4, block_tables, seq_lens, out, sm_scale=sm_scale,

@@ -342,3 +342,37 @@ def test_validation_errors_match_reference_messages():
         flashdec_b200.paged_decode_attention_into(q, k, k, bt, sl, torch.empty_like(q),
                                                   append_k=torch.empty((1, 1, 64), device="cuda",
                                                                        dtype=torch.float16))
+
+
+def test_prepared_signature_reuses_checks_but_reads_new_data():
+    """Calls with an already-seen signature take the prepared launch: new
+    values in new tensors (q, caches, block tables, lengths) are read, and
+    arguments outside the prepared case still get the reference's errors."""
+    from flashdec_b200.kernels import paged_decode as pd
+
+    c1 = cases.make_attn_case("split_257_193")
+    rng = np.random.default_rng(123)
+    for trial in range(3):
+        c = dict(c1)
+        if trial:
+            c["q"] = cases._normal(rng, c1["q"].shape, c1["dtype"])
+            c["k_cache"] = cases._normal(rng, c1["k_cache"].shape, c1["dtype"])
+            c["v_cache"] = cases._normal(rng, c1["v_cache"].shape, c1["dtype"])
+            order = rng.permutation(c1["k_cache"].shape[0])
+            c["block_tables"] = np.where(c1["block_tables"] >= 0, order[c1["block_tables"]], -1
+                                         ).astype(np.int32)
+            c["seq_lens"] = np.asarray([255 - trial, 190 + trial], np.int32)
+        q = to_dev(c["q"], c["dtype"])
+        out = torch.empty_like(q)
+        pd.paged_decode_attention_into(q, to_dev(c["k_cache"], c["dtype"]),
+                                       to_dev(c["v_cache"], c["dtype"]),
+                                       to_dev(c["block_tables"]), to_dev(c["seq_lens"]), out)
+        want = paged_decode_attention_ref(c["q"], c["k_cache"], c["v_cache"], c["block_tables"],
+                                          c["seq_lens"])
+        assert_attention_close(to_np(out), want)
+    assert len(pd._PREPARED) >= 1
+    with pytest.raises(ValueError, match="num_splits must be a positive integer"):
+        pd.paged_decode_attention_into(q, to_dev(c1["k_cache"], c1["dtype"]),
+                                       to_dev(c1["v_cache"], c1["dtype"]),
+                                       to_dev(c1["block_tables"]), to_dev(c1["seq_lens"]), out,
+                                       num_splits=True)
