@@ -50,12 +50,14 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kMaxRows = 16;  // query heads per head block (mma M)
 constexpr int kMaxStages = 16;
-constexpr int kMiscInts = 16;  // [0] abort, [1] ticket winner, [8..9] cluster mbarrier
+constexpr int kMiscInts = 16;  // [0] abort, [1] ticket winner, [2] stream-K cut test,
+                               // [8..9] cluster mbarrier
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kBarConsumers = 1;  // named barrier id for the consumer warps
 constexpr int kMergeBatch = 10;   // partials merged per register batch
 constexpr int kMaxClusterSize = 8;  // portable thread-block cluster size
+constexpr int kSnapSlackTiles = 16; // stream-K: extra tiles tolerated for pair-aligned cuts
 
 struct AttnParams {
   int num_seqs, num_q_heads, num_kv_heads, block_size, num_blocks, max_blocks;
@@ -162,24 +164,10 @@ struct Segment {
   int c_first;    // stream-K: first contributing CTA
 };
 
-struct Sched {
-  const int* prefix;  // smem, tiles prefix over sequences [num_seqs + 1]
-  const int* seqn;    // smem, attended tokens per sequence [num_seqs]
-  int64_t U;          // total tiles of the batch
-  int g;              // CTAs that own work (<= gridDim.x)
-  int64_t x, hi;      // this CTA's cursor / end (stream-K)
-  int done;           // split mode: the single segment was produced
-  __device__ __forceinline__ int64_t lo(int c) const { return (static_cast<int64_t>(c) * U) / g; }
-  // CTA owning linear tile x (largest c with lo(c) <= x)
-  __device__ __forceinline__ int owner(int64_t x_) const {
-    return static_cast<int>(((x_ + 1) * g + U - 1) / U) - 1;
-  }
-};
-
+// Largest b with nhb * prefix[b] <= x; empty sequences before a non-empty
+// one share its start, and the search lands on the last of them, i.e. the
+// non-empty one that actually contains x.
 __device__ __forceinline__ int find_seq(const int* prefix, int num_seqs, int nhb, int64_t x) {
-  // largest b with nhb * prefix[b] <= x; empty sequences before a non-empty
-  // one share its start, and the search lands on the last of them, i.e. the
-  // non-empty one that actually contains x.
   int lo = 0, hi = num_seqs - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -187,6 +175,45 @@ __device__ __forceinline__ int find_seq(const int* prefix, int num_seqs, int nhb
   }
   return lo;
 }
+
+struct Sched {
+  const int* prefix;  // smem, tiles prefix over sequences [num_seqs + 1]
+  const int* seqn;    // smem, attended tokens per sequence [num_seqs]
+  int num_seqs, nhb;
+  int64_t U;          // total tiles of the batch
+  int g;              // CTAs that own work (<= gridDim.x)
+  int64_t x, hi;      // this CTA's cursor / end (stream-K)
+  int done;           // split mode: the single segment was produced
+  const int* cut;     // smem, start of every CTA's range [g + 1] (stream-K; U < 2^31)
+  // Start of CTA c's tile range.  The ideal cut c * U / g is moved to the
+  // nearer end of the (sequence, head block) pair it falls in whenever that
+  // pair is no longer than a CTA's average share U / g: splitting a short
+  // pair costs a partial write, a ticket and a merge, while snapping shifts
+  // at most half a short pair between two neighbours.  Long pairs are cut
+  // where the ideal boundary falls.  The cuts stay non-decreasing (two ideal
+  // cuts are U / g apart, so they never share a short pair).
+  __device__ __forceinline__ int64_t snapped_cut(int c) const {
+    if (c <= 0) return 0;
+    if (c >= g) return U;
+    const int64_t xc = (static_cast<int64_t>(c) * U) / g;
+    const int b = find_seq(prefix, num_seqs, nhb, xc);
+    const int tiles = prefix[b + 1] - prefix[b];
+    if (tiles <= 0 || static_cast<int64_t>(tiles) * g > U) return xc;
+    const int64_t base = static_cast<int64_t>(nhb) * prefix[b];
+    const int64_t ps = base + ((xc - base) / tiles) * tiles;
+    const int64_t pe = ps + tiles;
+    return (xc - ps <= pe - xc) ? ps : pe;
+  }
+  // CTA owning linear tile x: the largest c < g with cut[c] <= x.
+  __device__ __forceinline__ int owner(int64_t x_) const {
+    int lo_c = 0, hi_c = g - 1;
+    while (lo_c < hi_c) {
+      const int mid = (lo_c + hi_c + 1) >> 1;
+      if (cut[mid] <= x_) lo_c = mid; else hi_c = mid - 1;
+    }
+    return lo_c;
+  }
+};
 
 // Tiles of split `split` out of `tiles`: equal ranges when p.balanced
 // (within one tile), else the reference's cdiv chunks (paged_decode.py:405-411).
@@ -354,12 +381,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- schedule ----------------------------------------------------------
   Sched sc;
   sc.prefix = prefix;
+  sc.num_seqs = p.num_seqs;
+  sc.nhb = p.nhb;
   int* seqn = prefix + p.num_seqs + 1;
   sc.seqn = seqn;
   sc.U = 0;
   sc.g = 1;
   sc.x = sc.hi = 0;
   sc.done = 0;
+  sc.cut = nullptr;
   const bool streamk = (p.num_splits == 0);
   if (streamk) {
     for (int b = tid; b < p.num_seqs; b += kThreads) {
@@ -395,9 +425,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     int64_t g = (sc.U + p.min_tiles_per_cta - 1) / p.min_tiles_per_cta;
     if (g > static_cast<int64_t>(gridDim.x)) g = gridDim.x;
     sc.g = static_cast<int>(g < 1 ? 1 : g);
+    // Every CTA's range start, computed once, in parallel, into shared
+    // memory.  Pair-aligned cuts are kept only if the busiest CTA gets at
+    // most kSnapSlackTiles more than with the ideal cuts: a split pair costs
+    // a partial write, a ticket and a merge (about a dozen tiles of ingest),
+    // so a little imbalance is cheaper, a lot is not (ragged batches).
+    int* cut = seqn + p.num_seqs;
+    for (int c = tid; c <= sc.g; c += kThreads) cut[c] = static_cast<int>(sc.snapped_cut(c));
+    if (tid == 0) misc[2] = 0;
+    __syncthreads();
+    int worst = 0;
+    for (int c = tid; c < sc.g; c += kThreads) worst = max(worst, cut[c + 1] - cut[c]);
+    if (worst > 0) atomicMax(&misc[2], worst);
+    __syncthreads();
+    const int64_t ideal_worst = (sc.U + sc.g - 1) / sc.g;
+    if (static_cast<int64_t>(misc[2]) > ideal_worst + kSnapSlackTiles) {
+      __syncthreads();  // every thread has read misc[2] before the table changes
+      for (int c = tid; c <= sc.g; c += kThreads) {
+        cut[c] = static_cast<int>((static_cast<int64_t>(c) * sc.U) / sc.g);
+      }
+    }
+    sc.cut = cut;
+    __syncthreads();
     if (sc.U > 0 && static_cast<int>(blockIdx.x) < sc.g) {
-      sc.x = sc.lo(blockIdx.x);
-      sc.hi = sc.lo(blockIdx.x + 1);
+      sc.x = cut[blockIdx.x];
+      sc.hi = cut[blockIdx.x + 1];
     }
   }
 
@@ -574,8 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t4 = lane & 3;   // thread in group
   const int mi = lane >> 3;  // ldmatrix matrix index
   const int r8 = lane & 7;   // ldmatrix row
-  uint32_t iter = 0;  // tile counter (tile i is consumed by warp i % 4)
-  int cst = 0;        // (stage, phase parity) of tile `iter`
+  int cst = 0;        // (stage, phase parity) of the next tile
   uint32_t cph = 0;
   // ---- Q fragments (A operand, rows = query heads of the head block) ----
   uint32_t qf[D / 16][4];
@@ -652,8 +703,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = s.t0; t < s.t1; ++t) {
       const int stage = cst;
       const uint32_t phase = cph;
-      const bool mine = static_cast<int>(iter & (kConsumerWarps - 1)) == warp;
-      ++iter;
+      // each stage is always consumed by the same warp (stage % 4), so a warp
+      // waits on its stages' phases in order whatever the stage count
+      const bool mine = (stage & (kConsumerWarps - 1)) == warp;
       if (++cst == NST) {
         cst = 0;
         cph ^= 1u;
@@ -1478,18 +1530,22 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
     tma = get_cache_tensor_map(cd, plane ? &mv : &mk, plane ? p.vperm : p.kperm);
   }
 
-  const int sched_ints = (plan.splits == 0) ? (2 * a->num_seqs + 1) : 0;
+  // stream-K: tiles prefix and lengths per sequence, and the start of every
+  // CTA's range (grid + 1 entries; the batch has fewer than 2^31 tiles)
+  const int sched_ints = (plan.splits == 0) ? (2 * a->num_seqs + 1 + (grid + 1)) : 0;
+  if (plan.splits == 0 &&
+      static_cast<int64_t>(a->num_seqs) * dv.nhb * plan.cap_tiles >= (int64_t(1) << 31))
+    return FD_ERR_UNSUPPORTED;
   const size_t fixed = (D == 128 ? smem_bytes<128>(0, sched_ints) : smem_bytes<64>(0, sched_ints));
   const size_t stage_bytes = (D == 128 ? Smem<128>::kStageBytes : Smem<64>::kStageBytes) + 20;
   const size_t cap = static_cast<size_t>(dev->max_smem_optin);
   if (fixed + 2 * stage_bytes > cap) return FD_ERR_UNSUPPORTED;  // batch too large for the schedule
   int stages = static_cast<int>((cap - fixed) / stage_bytes);
   stages = std::min(stages, kMaxStages);
-  // Tile i uses stage i % stages and is consumed by warp i % kConsumerWarps.
-  // With stages a multiple of the consumer-warp count every stage is always
-  // consumed by the same warp, so each warp waits on a stage's phases in
-  // order and a parity wait can never alias a phase one ring ahead.
-  stages -= stages % kConsumerWarps;
+  // Tile i uses stage i % stages and is consumed by warp (stage % 4): every
+  // stage always belongs to the same warp, so each warp waits on a stage's
+  // phases in order and a parity wait can never alias a phase one ring
+  // ahead, for any stage count of at least four.
   if (stages < kConsumerWarps) return FD_ERR_UNSUPPORTED;
   p.num_stages = stages;
   const size_t smem = D == 128 ? smem_bytes<128>(stages, sched_ints) : smem_bytes<64>(stages, sched_ints);
