@@ -618,6 +618,54 @@ def run_c5(torch, device, args, num_layers=36, num_requests=16, prefix_tokens=40
             "note": "host-driven (Python engine per layer, no graph capture)"}
 
 
+def run_sweep(torch, device, stream):
+    """Decode latency over batch x context for the Qwen attention shape
+    (16q/2kv, D128, bs32, bf16), graph replay over rotating pools of at least
+    400 MB where the shape allows; one JSON line per point."""
+    from oracle.paged_attention import attention_bytes
+
+    import flashdec_b200
+
+    hq, hkv, d, bs = 16, 2, 128, 32
+    peak, _ = _peaks()
+    points = []
+    for batch in (1, 2, 4, 8, 16, 32, 64, 128):
+        for ctx in (1024, 4096, 16384):
+            if batch * ctx > 128 * 16384:
+                continue
+            nblk = ctx // bs
+            g = torch.Generator(device=device).manual_seed(batch * 7 + ctx)
+            per_pool = 2 * batch * nblk * hkv * bs * d * 2 * 2
+            npools = max(2, min(12, math.ceil(400e6 / per_pool)))
+            pools = []
+            for _ in range(npools):
+                k = torch.randn((batch * nblk, hkv, bs, d), device=device, dtype=torch.bfloat16,
+                                generator=g)
+                v = torch.randn_like(k)
+                bt = torch.randperm(batch * nblk, device=device, generator=g).reshape(
+                    batch, nblk).to(torch.int32)
+                q = torch.randn((batch, hq, d), device=device, dtype=torch.bfloat16, generator=g)
+                pools.append((q, k, v, bt, torch.empty_like(q)))
+            sl = torch.full((batch,), ctx, device=device, dtype=torch.int32)
+            state = {"i": 0}
+
+            def step():
+                q, k, v, bt, o = pools[state["i"] % len(pools)]
+                state["i"] += 1
+                flashdec_b200.paged_decode_attention_into(q, k, v, bt, sl, o)
+
+            us = _graph_time_us(torch, stream, step, reps=20,
+                                inner=len(pools) * max(1, 24 // len(pools)))
+            nbytes = attention_bytes([ctx] * batch, hq, hkv, d, bs)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            points.append({"batch": batch, "context": ctx, "us_per_step": round(us, 3),
+                           "hbm_gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+                           "pools": npools})
+            del pools
+            torch.cuda.empty_cache()
+    return points
+
+
 # ---------------------------------------------------------------------------
 # CPU reference (the numpy oracle restating flashdec/paged_reference.py)
 # ---------------------------------------------------------------------------
@@ -721,6 +769,9 @@ def main():
     ap.add_argument("--steps", type=int, default=120000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--sweep", action="store_true",
+                    help="print decode latency over batch x context (Qwen shape), one JSON "
+                         "line per point, and exit")
     ap.add_argument("--kernel-only", nargs="?", const="c2", default=None,
                     choices=["c2", "c3", "c4"],
                     help="time only one device-resident workload (no e2e or CPU legs): c2 "
@@ -735,6 +786,14 @@ def main():
         res = run_reference(args, rank, world)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.sweep:
+        import torch
+
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        for point in run_sweep(torch, device, torch.cuda.Stream(device)):
+            print(json.dumps({"sweep": "qwen-shape decode", **point}), flush=True)
         return
     if args.kernel_only in ("c3", "c4"):
         import torch
