@@ -71,7 +71,7 @@ struct AttnParams {
   int64_t ks0, ks1, ks2, ks3;
   void* v;
   int64_t vs0, vs1, vs2, vs3;
-  int kperm[3], vperm[3];  // tensor-map axis order (0 token, 1 head, 2 block)
+  int kperm[4], vperm[4];  // tensor-map axis order (0 token, 1 head, 2 block, 3 half)
   const void* bt;
   int bt64;
   int64_t bts0, bts1;
@@ -120,6 +120,29 @@ struct Smem {
 // Column of element (row, col) in a merge buffer of 128-float-aligned rows:
 // XOR with 8 * (row % 4) so that consecutive rows start on different banks.
 __device__ __forceinline__ int merge_col(int row, int col) { return col ^ ((row & 3) << 3); }
+
+// Stage tiles (one 32-token tile of K or V).  Default layout: D/64 halves of
+// [32 rows][64 dims], one TMA box per (page, half).  kPage16 (head_dim 128,
+// 16-token pages, one box per page plane): [page][half][16 rows][64 dims].
+// Both carry the TMA 128B swizzle, which depends only on the shared-memory
+// address (16-byte chunk index XOR address bits 7-9 = row % 8).
+template <bool kPage16>
+__device__ __forceinline__ uint32_t stage_row_base(int row, int half) {
+  if constexpr (kPage16) {
+    return (row >> 4) * 4096 + half * 2048 + (row & 15) * 128;
+  } else {
+    return half * (kTile * 128) + row * 128;
+  }
+}
+template <bool kPage16>
+__device__ __forceinline__ uint32_t stage_tile_offset(int row, int dim) {
+  const int dd = dim & 63;
+  return stage_row_base<kPage16>(row, dim >> 6) + (((dd >> 3) ^ (row & 7)) << 4) + ((dd & 7) << 1);
+}
+template <bool kPage16>
+__device__ __forceinline__ uint32_t stage_chunk_offset(int row, int chunk) {
+  return stage_row_base<kPage16>(row, chunk >> 3) + (((chunk & 7) ^ (row & 7)) << 4);
+}
 
 // Byte offset of element (row, dim) in a [32][D] tile stored as D/64 halves
 // of [32][64] with the TMA 128B swizzle (16-byte chunk index XOR row % 8).
@@ -323,13 +346,13 @@ __device__ __forceinline__ void store_out4(const AttnParams& p, int b, int h, in
 }
 
 __device__ __forceinline__ int tmap_coord(int axis, int kv_head, int blk) {
-  return axis == 0 ? 0 : (axis == 1 ? kv_head : blk);
+  return axis == 1 ? kv_head : (axis == 2 ? blk : 0);  // token and half start at 0
 }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <typename T, int D, bool kTma>
+template <typename T, int D, bool kTma, bool kPage16>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ AttnParams p,
                         const __grid_constant__ CUtensorMap tmap_k,
@@ -554,7 +577,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (__all_sync(0xffffffffu, ok)) {
-          if constexpr (kTma) {
+          if constexpr (kTma && kPage16) {
+            // one 4 KB box per (page, plane): 16 tokens x both 64-dim halves
+            const int nops = npage * 2;
+            for (int base = 0; base < nops; base += 32) {
+              const int op = base + lane;
+              const int page = op >> 1;
+              const int pblk = __shfl_sync(0xffffffffu, blk, page & 31);
+              if (op < nops && ((pages >> page) & 1u)) {
+                const int plane = op & 1;  // 0: K, 1: V
+                uint32_t ph;
+                const int stage = stage_of(page >> 1, ph);
+                const uint32_t dst = smem_u32(stages + stage * SM::kStageBytes) +
+                                     plane * (SM::kHalves * SM::kHalfBytes) + (page & 1) * 4096;
+                const int* perm = plane ? p.vperm : p.kperm;
+                tma_load_5d(dst, plane ? &tmap_v : &tmap_k, smem_u32(&full_bar[stage]), 0,
+                            tmap_coord(perm[0], kv_head, pblk), tmap_coord(perm[1], kv_head, pblk),
+                            tmap_coord(perm[2], kv_head, pblk), tmap_coord(perm[3], kv_head, pblk),
+                            policy);
+              }
+            }
+          } else if constexpr (kTma) {
             const int nops = npage * kOps;
             for (int base = 0; base < nops; base += 32) {
               const int op = base + lane;
@@ -593,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int e = lane; e < bs * D; e += 32) {
                 const int r = e / D;
                 const int d = e - r * D;
-                const uint32_t off = tile_offset(j * bs + r, d);
+                const uint32_t off = stage_tile_offset<kPage16>(j * bs + r, d);
                 *reinterpret_cast<uint16_t*>(sb + off) = kp[r * p.ks2 + d * p.ks3];
                 *reinterpret_cast<uint16_t*>(sb + SM::kHalves * SM::kHalfBytes + off) =
                     vp[r * p.vs2 + d * p.vs3];
@@ -732,7 +775,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r = e / (D / 8);
           const int c = e - r * (D / 8);
           if ((inv >> r) & 1u) {
-            *reinterpret_cast<uint4*>(sb + SM::kHalves * SM::kHalfBytes + chunk_offset(r, c)) =
+            *reinterpret_cast<uint4*>(sb + SM::kHalves * SM::kHalfBytes +
+                                      stage_chunk_offset<kPage16>(r, c)) =
                 make_uint4(0u, 0u, 0u, 0u);
           }
         }
@@ -753,8 +797,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int d = lane; d < D; d += 32) {
           const T kv = akp[d * p.aks2];
           const T vv = avp[d * p.avs2];
-          *reinterpret_cast<T*>(sb + tile_offset(ra, d)) = kv;
-          *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes + tile_offset(ra, d)) = vv;
+          *reinterpret_cast<T*>(sb + stage_tile_offset<kPage16>(ra, d)) = kv;
+          *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes +
+                                stage_tile_offset<kPage16>(ra, d)) = vv;
           if (store) {
             kc[d * p.ks3] = kv;
             vc[d * p.vs3] = vv;
@@ -776,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tok = np * 16 + (mi >> 1) * 8 + r8;
           const int chunk = ks * 2 + (mi & 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4(kbase + chunk_offset(tok, chunk), b0a, b1a, b0b, b1b);
+          ldsm_x4(kbase + stage_chunk_offset<kPage16>(tok, chunk), b0a, b1a, b0b, b1b);
           mma_16816<T>(sacc[2 * np], qf[ks], b0a, b1a);
           mma_16816<T>(sacc[2 * np + 1], qf[ks], b0b, b1b);
         }
@@ -843,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tok = kk * 16 + (mi & 1) * 8 + r8;
           const int chunk = dp * 2 + (mi >> 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4_t(vbase + chunk_offset(tok, chunk), b0a, b1a, b0b, b1b);
+          ldsm_x4_t(vbase + stage_chunk_offset<kPage16>(tok, chunk), b0a, b1a, b0b, b1b);
           mma_16816<T>(o[2 * dp], a, b0a, b1a);
           mma_16816<T>(o[2 * dp + 1], a, b0b, b1b);
         }
@@ -1319,10 +1364,10 @@ int max_active_clusters(K kern, size_t smem, int size, const DeviceInfo& dev) {
   return n;
 }
 
-template <typename T, int D, bool kTma>
+template <typename T, int D, bool kTma, bool kPage16>
 int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
            size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
-  auto kern = paged_decode_kernel<T, D, kTma>;
+  auto kern = paged_decode_kernel<T, D, kTma, kPage16>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   const int slot = dev.device & 63;
@@ -1373,8 +1418,12 @@ int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 gr
 template <typename T, int D>
 int dispatch_tma(bool tma, const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
                  dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
-  return tma ? launch<T, D, true>(prm, mk, mv, grid, smem, dev, st)
-             : launch<T, D, false>(prm, mk, mv, grid, smem, dev, st);
+  if (!tma) return launch<T, D, false, false>(prm, mk, mv, grid, smem, dev, st);
+  if constexpr (D == 128) {
+    // whole-plane boxes (5-D maps) for 16-token pages
+    if (prm.kperm[3] >= 0) return launch<T, D, true, true>(prm, mk, mv, grid, smem, dev, st);
+  }
+  return launch<T, D, true, false>(prm, mk, mv, grid, smem, dev, st);
 }
 
 }  // namespace

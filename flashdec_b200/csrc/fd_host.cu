@@ -59,7 +59,7 @@ struct MapKey {
 struct MapEntry {
   MapKey key;
   CUtensorMap map;
-  int perm[3];
+  int perm[4];
   uint64_t stamp;
 };
 
@@ -127,7 +127,7 @@ int cuda_status(cudaError_t e) {
   return FD_ERR_CUDA;
 }
 
-bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]) {
+bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
   if (d.elem_bytes != 2 || d.stride[3] != 1) return false;
   if (d.head_dim != 64 && d.head_dim != 128) return false;
   if (reinterpret_cast<uintptr_t>(d.base) % 16 != 0) return false;
@@ -143,7 +143,7 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]) {
       if (e.key == key) {
         e.stamp = ++g_map_clock;
         *out = e.map;
-        std::copy(e.perm, e.perm + 3, perm);
+        std::copy(e.perm, e.perm + 4, perm);
         return true;
       }
     }
@@ -151,7 +151,11 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]) {
   resolve_encoder();
   if (!g_encode) return false;
 
-  // outer axes: 0 token (box = block_size), 1 head (box 1), 2 block (box 1)
+  // Outer axes: 0 token (box = block_size), 1 head (box 1), 2 block (box 1),
+  // sorted by stride.  With head_dim 128 and 16-token pages the two 64-dim
+  // halves are one more axis (id 3, stride 128 bytes, box 2) right after the
+  // token axis, so one 4 KB box holds a whole page plane ([half][16][64] in
+  // shared memory) instead of two 2 KB boxes.
   struct Axis {
     int id;
     uint64_t size;
@@ -166,20 +170,34 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]) {
   }};
   std::stable_sort(ax.begin(), ax.end(),
                    [](const Axis& a, const Axis& b) { return a.stride_bytes < b.stride_bytes; });
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d.head_dim), ax[0].size, ax[1].size, ax[2].size};
-  cuuint64_t strides[3] = {ax[0].stride_bytes, ax[1].stride_bytes, ax[2].stride_bytes};
-  cuuint32_t box[4] = {64u, ax[0].box, ax[1].box, ax[2].box};
-  cuuint32_t estride[4] = {1u, 1u, 1u, 1u};
+  const bool halves = d.head_dim == 128 && d.block_size == 16;
+  std::array<Axis, 4> all;
+  int n = 0;
+  for (const Axis& a : ax) {
+    all[n++] = a;
+    if (a.id == 0 && halves) all[n++] = Axis{3, 2u, 128u, 2u};
+  }
+  const int rank = 1 + n;
+  cuuint64_t dims[5] = {halves ? 64u : static_cast<cuuint64_t>(d.head_dim), 0, 0, 0, 0};
+  cuuint64_t strides[4] = {0, 0, 0, 0};
+  cuuint32_t box[5] = {64u, 1u, 1u, 1u, 1u};
+  cuuint32_t estride[5] = {1u, 1u, 1u, 1u, 1u};
+  int pm[4] = {-1, -1, -1, -1};
+  for (int i = 0; i < n; ++i) {
+    dims[i + 1] = all[i].size;
+    strides[i] = all[i].stride_bytes;
+    box[i + 1] = all[i].box;
+    pm[i] = all[i].id;
+  }
   CUtensorMap map;
   CUresult r = g_encode(&map,
                         d.is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        4, const_cast<void*>(d.base),
+                        static_cast<cuuint32_t>(rank), const_cast<void*>(d.base),
                         dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
-  int pm[3] = {ax[0].id, ax[1].id, ax[2].id};
   {
     std::lock_guard<std::mutex> lock(g_map_mu);
     if (g_maps.size() >= kMapCacheSize) {
@@ -192,12 +210,12 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]) {
     MapEntry e;
     e.key = key;
     e.map = map;
-    std::copy(pm, pm + 3, e.perm);
+    std::copy(pm, pm + 4, e.perm);
     e.stamp = ++g_map_clock;
     g_maps.push_back(e);
   }
   *out = map;
-  std::copy(pm, pm + 3, perm);
+  std::copy(pm, pm + 4, perm);
   return true;
 }
 

@@ -34,12 +34,15 @@ struct CacheDesc {
   int64_t stride[4];    // block, head, token, dim (elements)
 };
 
-// Encode (or fetch from the cache) a 4-D tiled tensor map over `d` with a box
-// of [64 dims x block_size tokens x 1 head x 1 block] and 128B swizzle.
-// `perm[i]` receives which logical axis (0 token, 1 head, 2 block) is tensor
-// map dimension i+1 (outer dims sorted by ascending stride).
-// Returns false when the layout cannot be described by a tensor map.
-bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[3]);
+// Encode (or fetch from the cache) a tiled tensor map over `d` with 128B
+// swizzle whose box is one page plane: [64 dims x block_size tokens x 1 head
+// x 1 block] (4-D), or, for head_dim 128 with 16-token pages, the same plus a
+// "64-dim half" axis of box 2 (5-D) so one 4 KB copy moves the whole plane.
+// `perm[i]` receives which axis tensor-map dimension i+1 is (0 token, 1 head,
+// 2 block, 3 half; -1 unused); outer axes are sorted by ascending stride and
+// the half axis follows the token axis.  Returns false when the layout cannot
+// be described by a tensor map.
+bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]);
 
 // FD_OK, or FD_ERR_CUDA with the message kept for fd_error_string.
 int cuda_status(cudaError_t e);
