@@ -121,27 +121,31 @@ struct Smem {
 // XOR with 8 * (row % 4) so that consecutive rows start on different banks.
 __device__ __forceinline__ int merge_col(int row, int col) { return col ^ ((row & 3) << 3); }
 
-// Stage tiles (one 32-token tile of K or V).  Default layout: D/64 halves of
-// [32 rows][64 dims], one TMA box per (page, half).  kPage16 (head_dim 128,
-// 16-token pages, one box per page plane): [page][half][16 rows][64 dims].
-// Both carry the TMA 128B swizzle, which depends only on the shared-memory
-// address (16-byte chunk index XOR address bits 7-9 = row % 8).
-template <bool kPage16>
+// Stage tiles (one 32-token tile of K or V).  Default layout (kPageRows 0):
+// D/64 halves of [32 rows][64 dims], one TMA box per (page, half).  With
+// kPageRows = 16 or 8 (head_dim 128, pages of that many tokens, one box per
+// page plane): [page][half][kPageRows rows][64 dims].  Both carry the TMA
+// 128B swizzle, which depends only on the shared-memory address (16-byte
+// chunk index XOR address bits 7-9 = row % 8; every half of a page starts on
+// a 1 KB boundary).
+template <int kPageRows>
 __device__ __forceinline__ uint32_t stage_row_base(int row, int half) {
-  if constexpr (kPage16) {
-    return (row >> 4) * 4096 + half * 2048 + (row & 15) * 128;
+  if constexpr (kPageRows > 0) {
+    return (row / kPageRows) * (kPageRows * 256) + half * (kPageRows * 128) +
+           (row % kPageRows) * 128;
   } else {
     return half * (kTile * 128) + row * 128;
   }
 }
-template <bool kPage16>
+template <int kPageRows>
 __device__ __forceinline__ uint32_t stage_tile_offset(int row, int dim) {
   const int dd = dim & 63;
-  return stage_row_base<kPage16>(row, dim >> 6) + (((dd >> 3) ^ (row & 7)) << 4) + ((dd & 7) << 1);
+  return stage_row_base<kPageRows>(row, dim >> 6) + (((dd >> 3) ^ (row & 7)) << 4) +
+         ((dd & 7) << 1);
 }
-template <bool kPage16>
+template <int kPageRows>
 __device__ __forceinline__ uint32_t stage_chunk_offset(int row, int chunk) {
-  return stage_row_base<kPage16>(row, chunk >> 3) + (((chunk & 7) ^ (row & 7)) << 4);
+  return stage_row_base<kPageRows>(row, chunk >> 3) + (((chunk & 7) ^ (row & 7)) << 4);
 }
 
 // Byte offset of element (row, dim) in a [32][D] tile stored as D/64 halves
@@ -352,7 +356,7 @@ __device__ __forceinline__ int tmap_coord(int axis, int kv_head, int blk) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <typename T, int D, bool kTma, bool kPage16>
+template <typename T, int D, bool kTma, int kPageRows>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ AttnParams p,
                         const __grid_constant__ CUtensorMap tmap_k,
@@ -577,8 +581,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (__all_sync(0xffffffffu, ok)) {
-          if constexpr (kTma && kPage16) {
-            // one 4 KB box per (page, plane): 16 tokens x both 64-dim halves
+          if constexpr (kTma && kPageRows > 0) {
+            // one box per (page, plane): kPageRows tokens x both 64-dim halves
             const int nops = npage * 2;
             for (int base = 0; base < nops; base += 32) {
               const int op = base + lane;
@@ -587,9 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (op < nops && ((pages >> page) & 1u)) {
                 const int plane = op & 1;  // 0: K, 1: V
                 uint32_t ph;
-                const int stage = stage_of(page >> 1, ph);
+                const int stage = stage_of(page >> ppt_shift, ph);
                 const uint32_t dst = smem_u32(stages + stage * SM::kStageBytes) +
-                                     plane * (SM::kHalves * SM::kHalfBytes) + (page & 1) * 4096;
+                                     plane * (SM::kHalves * SM::kHalfBytes) +
+                                     (page & (PPT - 1)) * (kPageRows * 256);
                 const int* perm = plane ? p.vperm : p.kperm;
                 tma_load_5d(dst, plane ? &tmap_v : &tmap_k, smem_u32(&full_bar[stage]), 0,
                             tmap_coord(perm[0], kv_head, pblk), tmap_coord(perm[1], kv_head, pblk),
@@ -636,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int e = lane; e < bs * D; e += 32) {
                 const int r = e / D;
                 const int d = e - r * D;
-                const uint32_t off = stage_tile_offset<kPage16>(j * bs + r, d);
+                const uint32_t off = stage_tile_offset<kPageRows>(j * bs + r, d);
                 *reinterpret_cast<uint16_t*>(sb + off) = kp[r * p.ks2 + d * p.ks3];
                 *reinterpret_cast<uint16_t*>(sb + SM::kHalves * SM::kHalfBytes + off) =
                     vp[r * p.vs2 + d * p.vs3];
@@ -776,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int c = e - r * (D / 8);
           if ((inv >> r) & 1u) {
             *reinterpret_cast<uint4*>(sb + SM::kHalves * SM::kHalfBytes +
-                                      stage_chunk_offset<kPage16>(r, c)) =
+                                      stage_chunk_offset<kPageRows>(r, c)) =
                 make_uint4(0u, 0u, 0u, 0u);
           }
         }
@@ -797,9 +802,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int d = lane; d < D; d += 32) {
           const T kv = akp[d * p.aks2];
           const T vv = avp[d * p.avs2];
-          *reinterpret_cast<T*>(sb + stage_tile_offset<kPage16>(ra, d)) = kv;
+          *reinterpret_cast<T*>(sb + stage_tile_offset<kPageRows>(ra, d)) = kv;
           *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes +
-                                stage_tile_offset<kPage16>(ra, d)) = vv;
+                                stage_tile_offset<kPageRows>(ra, d)) = vv;
           if (store) {
             kc[d * p.ks3] = kv;
             vc[d * p.vs3] = vv;
@@ -821,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tok = np * 16 + (mi >> 1) * 8 + r8;
           const int chunk = ks * 2 + (mi & 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4(kbase + stage_chunk_offset<kPage16>(tok, chunk), b0a, b1a, b0b, b1b);
+          ldsm_x4(kbase + stage_chunk_offset<kPageRows>(tok, chunk), b0a, b1a, b0b, b1b);
           mma_16816<T>(sacc[2 * np], qf[ks], b0a, b1a);
           mma_16816<T>(sacc[2 * np + 1], qf[ks], b0b, b1b);
         }
@@ -888,7 +893,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tok = kk * 16 + (mi & 1) * 8 + r8;
           const int chunk = dp * 2 + (mi >> 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4_t(vbase + stage_chunk_offset<kPage16>(tok, chunk), b0a, b1a, b0b, b1b);
+          ldsm_x4_t(vbase + stage_chunk_offset<kPageRows>(tok, chunk), b0a, b1a, b0b, b1b);
           mma_16816<T>(o[2 * dp], a, b0a, b1a);
           mma_16816<T>(o[2 * dp + 1], a, b0b, b1b);
         }
@@ -1364,10 +1369,10 @@ int max_active_clusters(K kern, size_t smem, int size, const DeviceInfo& dev) {
   return n;
 }
 
-template <typename T, int D, bool kTma, bool kPage16>
+template <typename T, int D, bool kTma, int kPageRows>
 int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
            size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
-  auto kern = paged_decode_kernel<T, D, kTma, kPage16>;
+  auto kern = paged_decode_kernel<T, D, kTma, kPageRows>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   const int slot = dev.device & 63;
@@ -1418,12 +1423,15 @@ int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 gr
 template <typename T, int D>
 int dispatch_tma(bool tma, const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
                  dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
-  if (!tma) return launch<T, D, false, false>(prm, mk, mv, grid, smem, dev, st);
+  if (!tma) return launch<T, D, false, 0>(prm, mk, mv, grid, smem, dev, st);
   if constexpr (D == 128) {
-    // whole-plane boxes (5-D maps) for 16-token pages
-    if (prm.kperm[3] >= 0) return launch<T, D, true, true>(prm, mk, mv, grid, smem, dev, st);
+    // whole-plane boxes (5-D maps) for 16- and 8-token pages
+    if (prm.kperm[3] >= 0) {
+      return prm.block_size == 16 ? launch<T, D, true, 16>(prm, mk, mv, grid, smem, dev, st)
+                                  : launch<T, D, true, 8>(prm, mk, mv, grid, smem, dev, st);
+    }
   }
-  return launch<T, D, true, false>(prm, mk, mv, grid, smem, dev, st);
+  return launch<T, D, true, 0>(prm, mk, mv, grid, smem, dev, st);
 }
 
 }  // namespace

@@ -152,10 +152,10 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
   if (!g_encode) return false;
 
   // Outer axes: 0 token (box = block_size), 1 head (box 1), 2 block (box 1),
-  // sorted by stride.  With head_dim 128 and 16-token pages the two 64-dim
-  // halves are one more axis (id 3, stride 128 bytes, box 2) right after the
-  // token axis, so one 4 KB box holds a whole page plane ([half][16][64] in
-  // shared memory) instead of two 2 KB boxes.
+  // sorted by stride.  With head_dim 128 and 16- or 8-token pages the two
+  // 64-dim halves are one more axis (id 3, stride 128 bytes, box 2) right
+  // after the token axis, so one box holds a whole page plane
+  // ([half][block_size][64] in shared memory) instead of two half-size boxes.
   struct Axis {
     int id;
     uint64_t size;
@@ -170,7 +170,7 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
   }};
   std::stable_sort(ax.begin(), ax.end(),
                    [](const Axis& a, const Axis& b) { return a.stride_bytes < b.stride_bytes; });
-  const bool halves = d.head_dim == 128 && d.block_size == 16;
+  const bool halves = d.head_dim == 128 && (d.block_size == 16 || d.block_size == 8);
   std::array<Axis, 4> all;
   int n = 0;
   for (const Axis& a : ax) {

@@ -36,8 +36,8 @@ struct CacheDesc {
 
 // Encode (or fetch from the cache) a tiled tensor map over `d` with 128B
 // swizzle whose box is one page plane: [64 dims x block_size tokens x 1 head
-// x 1 block] (4-D), or, for head_dim 128 with 16-token pages, the same plus a
-// "64-dim half" axis of box 2 (5-D) so one 4 KB copy moves the whole plane.
+// x 1 block] (4-D), or, for head_dim 128 with 16- or 8-token pages, the same
+// plus a "64-dim half" axis of box 2 (5-D) so one copy moves the whole plane.
 // `perm[i]` receives which axis tensor-map dimension i+1 is (0 token, 1 head,
 // 2 block, 3 half; -1 unused); outer axes are sorted by ascending stride and
 // the half axis follows the token axis.  Returns false when the layout cannot
