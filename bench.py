@@ -813,6 +813,9 @@ def main():
     if world > 1:
         from datetime import timedelta
 
+        # rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
