@@ -8,30 +8,37 @@
 // Work decomposition.  The unit of work is a 32-token tile of one
 // (sequence, head block) pair; a head block is up to 16 query heads that share
 // one KV head, so every K/V byte is read once per head block (once per KV head
-// whenever the GQA group is <= 16).  Two schedules:
-//   * num_splits == 0 (auto): the tiles of the whole batch are laid out in
-//     (sequence, head block, tile) order and cut into equal ranges, one per
-//     persistent CTA.  A CTA's range may cover the tail of one pair, whole
-//     pairs and the head of another; every piece is a "segment".  This
-//     balances ragged batches to within one tile per SM.
+// whenever the GQA group is <= 16).  Schedules:
+//   * num_splits == 0 (auto), large batches: the tiles of the whole batch are
+//     laid out in (sequence, head block, tile) order and cut into near-equal
+//     ranges, one per persistent CTA; cuts that fall inside a short pair move
+//     to its boundary when that costs little balance.  A CTA's range may
+//     cover the tail of one pair, whole pairs and the head of another; every
+//     piece is a "segment".  Ragged batches balance to within a tile per SM.
+//   * num_splits == 0 (auto), small batches: every pair is split into S equal
+//     ranges (3-D grid split x head block x sequence).  When all pairs fit as
+//     co-resident thread-block clusters, the S CTAs of a pair form one
+//     cluster and merge through distributed shared memory.
 //   * num_splits == S: the reference's fixed split of every sequence into S
 //     chunks of cdiv(tiles, S) tiles (paged_decode.py:395-411), one CTA each.
-// A segment that covers a whole pair writes the output directly.  Otherwise
-// it writes an un-normalised partial (acc, max, sum) and takes a ticket; the
-// CTA that takes the last ticket of the pair merges all partials (the reducer
-// runs inside the kernel: no second launch and no CTA ever waits for another)
-// and re-arms the ticket for the next call.
+// A segment that covers a whole pair writes the output directly.  In a
+// cluster, each CTA pushes its rows' (max, sum, acc) into the row owner's
+// shared memory and the owner merges them.  Otherwise a segment writes an
+// un-normalised partial to global memory and takes a ticket; the CTA that
+// takes the last ticket of the pair merges all partials (no second launch, no
+// CTA ever waits for another) and re-arms the ticket for the next call.
 //
 // Inside a CTA: warp 4 is the producer.  It resolves block-table entries
-// (32 at a time, one per lane) and issues one TMA box per (page, 64-dim half)
-// into a ring of shared-memory stages (128B swizzle; one "full" and one
-// "empty" mbarrier per stage).  Caches whose strides a tensor map cannot
-// describe are copied by the producer warp with ordinary loads instead.
-// Warps 0-3 are consumers: each takes whole tiles round robin and runs
-// S = Q K^T and O += P V on the tensor cores (mma.sync m16n8k16, fp32
-// accumulate) with an online softmax in fp32 (base-2 exponent, scale folded
-// in).  At the end of a segment the four warps' (m, l, O) are merged through
-// shared memory.
+// (32 at a time, one per lane) and issues TMA boxes into a ring of
+// shared-memory stages (128B swizzle; one "full" and one "empty" mbarrier per
+// stage): one box per (page, 64-dim half), or for head_dim 128 with 16- or
+// 8-token pages one box per page plane through a 5-D map.  Caches whose
+// strides a tensor map cannot describe are copied by the producer warp with
+// ordinary loads instead.  Warps 0-3 are consumers: each owns the stages
+// s with s % 4 == warp and runs S = Q K^T and O += P V on the tensor cores
+// (mma.sync m16n8k16, fp32 accumulate) with an online softmax in fp32
+// (base-2 exponent, scale folded in).  At the end of a segment the four
+// warps' (m, l, O) are merged through shared memory.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
