@@ -21,6 +21,7 @@ import math
 from dataclasses import dataclass, replace
 from typing import Hashable
 
+import numpy as np
 import torch
 
 from . import _native
@@ -45,27 +46,83 @@ class KVTokenTransactionView:
 
 class _DeviceMeta:
     """Device copies of one transaction's metadata: ``kernel`` tensors are
-    private (the kernels read only these), ``public`` ones back the views."""
+    private (the kernels read only these), ``public`` ones back the views.
 
-    def __init__(self, device, positions, locations, block_table_rows):
+    The per-token integers (positions, block ids, offsets as int64 and the
+    effective lengths as int32) travel as one packed byte buffer: one pinned
+    staging copy, one host-to-device copy.  The block table comes from
+    :class:`_BlockTableCache` and is shared with earlier transactions while
+    its rows are unchanged."""
+
+    def __init__(self, device, positions, locations, table):
         n = len(positions)
-        i64 = torch.tensor([*positions, *(b for b, _ in locations), *(o for _, o in locations)],
-                           dtype=torch.int64)
-        i32 = torch.tensor([*(p + 1 for p in positions), *(x for row in block_table_rows for x in row)],
-                           dtype=torch.int32)
+        packed = np.empty(3 * n * 8 + n * 4, np.uint8)
+        i64 = packed[:3 * n * 8].view(np.int64)
+        i64[:n] = positions
+        i64[n:2 * n] = [b for b, _ in locations]
+        i64[2 * n:] = [o for _, o in locations]
+        packed[3 * n * 8:].view(np.int32)[:] = i64[:n] + 1
+        buf = torch.from_numpy(packed)
         if device.type == "cuda":
-            i64 = i64.pin_memory().to(device, non_blocking=True)
-            i32 = i32.pin_memory().to(device, non_blocking=True)
-        width = len(block_table_rows[0]) if block_table_rows else 1
-        self.positions = i64[:n]
-        self.block_ids = i64[n:2 * n]
-        self.offsets = i64[2 * n:3 * n]
-        self.eff_seq_lens = i32[:n]
-        self.block_tables = i32[n:].view(n, width)
-        p64, p32 = i64.clone(), i32.clone()
-        self.public = dict(positions=p64[:n], physical_block_ids=p64[n:2 * n],
-                           block_offsets=p64[2 * n:3 * n], effective_seq_lens=p32[:n],
-                           block_tables=p32[n:].view(n, width))
+            buf = buf.pin_memory().to(device, non_blocking=True)
+        self._packed, self.block_tables = buf, table
+        (self.positions, self.block_ids, self.offsets,
+         self.eff_seq_lens) = _unpack_meta(buf, n)
+        self.public = self.snapshot()
+
+    def snapshot(self):
+        """Fresh copies of the metadata (two copies: packed integers, table)."""
+        pub = _unpack_meta(self._packed.clone(), len(self.positions))
+        return dict(positions=pub[0], physical_block_ids=pub[1], block_offsets=pub[2],
+                    effective_seq_lens=pub[3], block_tables=self.block_tables.clone())
+
+
+def _unpack_meta(buf, n):
+    """(positions, block ids, offsets) int64 and effective lengths int32 views
+    of a packed metadata buffer."""
+    i64 = buf[:3 * n * 8].view(torch.int64)
+    return i64[:n], i64[n:2 * n], i64[2 * n:], buf[3 * n * 8:].view(torch.int32)
+
+
+class _BlockTableCache:
+    """Block table of the last transaction, kept on the device.
+
+    Decode steps usually repeat the same request rows and a row only changes
+    when its request takes a new block (once per ``block_size`` tokens), so
+    rebuilding the padded table from Python lists every step would dominate
+    ``begin_token``.  Rows are compared against copies of the ledger's lists
+    (exact), changed rows are patched into a copy of the previous host array,
+    and an unchanged table is reused as is: a table is never written after
+    its upload, so transactions may share it."""
+
+    def __init__(self):
+        self.ids = None
+        self.rows = None
+        self.host = None
+        self.table = None
+
+    def get(self, device, ids, block_lists):
+        n = len(block_lists)
+        width = max(1, max(map(len, block_lists)))
+        if self.ids == ids and self.host is not None and self.host.shape[1] == width:
+            changed = [i for i, (a, b) in enumerate(zip(block_lists, self.rows)) if a != b]
+            if not changed:
+                return self.table
+            host = self.host.copy()
+        else:
+            changed = range(n)
+            host = np.empty((n, width), np.int32)
+        for i in changed:
+            row = block_lists[i]
+            host[i, :len(row)] = row
+            host[i, len(row):] = -1
+        table = torch.from_numpy(host)
+        if device.type == "cuda":
+            table = table.pin_memory().to(device, non_blocking=True)
+        else:
+            table = table.clone()
+        self.ids, self.rows, self.host, self.table = ids, [list(b) for b in block_lists], host, table
+        return table
 
 
 class _FusedLayerLauncher:
@@ -228,6 +285,7 @@ class PagedKVCache:
         self.k_cache = torch.zeros(shape, device=device, dtype=dtype)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.device = self.k_cache.device
+        self._tables = _BlockTableCache()
 
     # ----------------------------------------------------------- lifecycle
     def add_request(self, request_id):
@@ -354,8 +412,9 @@ class PagedKVCache:
         ids = tuple(self._normalize_request_ids(request_ids))
         tx = self._ledger.begin_token(ids)
         try:
-            rows = self._ledger.block_table_rows(ids)
-            tx.device_view = _DeviceMeta(self.device, tx.positions, tx.locations, rows)
+            table = self._tables.get(self.device, ids,
+                                     [self._ledger.requests[r].block_ids for r in ids])
+            tx.device_view = _DeviceMeta(self.device, tx.positions, tx.locations, table)
         except Exception:
             self._ledger.abort_token(tx)
             raise
@@ -462,6 +521,10 @@ class PagedKVCache:
         view = replace(self._view(state), state="aborted")
         self._ledger.abort_token(state)
         return view
+
+    def _transaction_snapshot(self, transaction):
+        """Fresh copies of an open transaction's public metadata tensors."""
+        return self._require_open_transaction(transaction).device_view.snapshot()
 
     def transaction_view(self, transaction):
         state = self._require_transaction(transaction)

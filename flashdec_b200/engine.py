@@ -264,12 +264,12 @@ class DecodeEngine:
             self._backpressure_count += 1
             raise RuntimeError("insufficient physical blocks to begin decode step")
         ctx = self.cache.begin_token(ids)
+        snap = self.cache._transaction_snapshot(ctx)  # the handle's own copies
         handle = DecodeStepTransaction(
             transaction_id=ctx.transaction_id, engine_version=self._state_version + 1,
-            request_ids=tuple(ids), positions=ctx.positions.clone(),
-            physical_block_ids=ctx.physical_block_ids.clone(),
-            block_offsets=ctx.block_offsets.clone(), block_tables=ctx.block_tables.clone(),
-            effective_seq_lens=ctx.effective_seq_lens.clone())
+            request_ids=tuple(ids), positions=snap["positions"],
+            physical_block_ids=snap["physical_block_ids"], block_offsets=snap["block_offsets"],
+            block_tables=snap["block_tables"], effective_seq_lens=snap["effective_seq_lens"])
         self._bump_state_version()
         self._open = _OpenStep(handle, ctx, needed)
         return handle
@@ -516,7 +516,8 @@ class DecodeEngine:
 
     def _needed_new_blocks(self, ids):
         bs = self.cache.block_size
-        return sum(self.cache.request_state(r)["seq_len"] % bs == 0 for r in ids)
+        ledger = self.cache._ledger
+        return sum(ledger.require_request(r).seq_len % bs == 0 for r in ids)
 
     def _normalize_waiting_ids(self, request_ids):
         if request_ids is None:
