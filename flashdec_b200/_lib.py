@@ -53,6 +53,8 @@ class PagedDecodeArgs(ctypes.Structure):
         ("part_stat_stride", _I64x3),
         ("tickets", _vp), ("tickets_capacity", _i64), ("scratch", _vp), ("scratch_bytes", _sz),
         ("max_ctas", _i32), ("min_tiles_per_cta", _i32),
+        ("rope_dim", _i32), ("rope_inv_freq", _vp), ("rope_positions", _vp),
+        ("rope_positions_index", _i32), ("rope_positions_stride", _i64),
     ]
 
 

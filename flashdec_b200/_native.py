@@ -134,13 +134,15 @@ class PreparedDecode:
 def prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, block_size,
                          num_seqs, num_splits=0, epilogue=_lib.FD_EPILOGUE_FUSED, append_k=None,
                          append_v=None, slot_mapping=None, partials=None, max_ctas=0,
-                         min_tiles_per_cta=0):
+                         min_tiles_per_cta=0, rope=None):
     """Fill the ``fd_paged_decode`` struct for these tensors and size the
     workspace; returns a :class:`PreparedDecode`.
 
     ``k4``/``v4`` are 4-D views in logical order [block, kv_head, token, dim]
     (any strides).  ``partials`` = (acc, max, sum) in the reference split
-    workspace layout, or None for the internal workspace.
+    workspace layout, or None for the internal workspace.  ``rope`` =
+    (rotary_dim, inv_freq, positions) rotates q and ``append_k`` in the
+    kernel (fused append only).
     """
     lib = _lib.load_library()
     a = _lib.PagedDecodeArgs()
@@ -176,6 +178,13 @@ def prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, bl
         a.slot_mapping = slot_mapping.data_ptr()
         a.slot_mapping_index = index_code(slot_mapping)
         a.slot_mapping_stride = slot_mapping.stride(0)
+    if rope is not None:
+        rotary_dim, inv_freq, positions = rope
+        a.rope_dim = int(rotary_dim)
+        a.rope_inv_freq = inv_freq.data_ptr()
+        a.rope_positions = positions.data_ptr()
+        a.rope_positions_index = index_code(positions)
+        a.rope_positions_stride = positions.stride(0)
     a.num_splits = int(num_splits)
     a.epilogue = int(epilogue)
     if partials is not None:

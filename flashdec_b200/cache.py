@@ -48,25 +48,27 @@ class _DeviceMeta:
     """Device copies of one transaction's metadata: ``kernel`` tensors are
     private (the kernels read only these), ``public`` ones back the views.
 
-    The per-token integers (positions, block ids, offsets as int64 and the
-    effective lengths as int32) travel as one packed byte buffer: one pinned
-    staging copy, one host-to-device copy.  The block table comes from
+    The per-token integers (positions, block ids, offsets and slots
+    ``block_id * block_size + offset`` as int64, the effective lengths as
+    int32) travel as one packed byte buffer: one pinned staging copy, one
+    host-to-device copy.  The block table comes from
     :class:`_BlockTableCache` and is shared with earlier transactions while
     its rows are unchanged."""
 
-    def __init__(self, device, positions, locations, table):
+    def __init__(self, device, positions, locations, table, block_size):
         n = len(positions)
-        packed = np.empty(3 * n * 8 + n * 4, np.uint8)
-        i64 = packed[:3 * n * 8].view(np.int64)
+        packed = np.empty(4 * n * 8 + n * 4, np.uint8)
+        i64 = packed[:4 * n * 8].view(np.int64)
         i64[:n] = positions
         i64[n:2 * n] = [b for b, _ in locations]
-        i64[2 * n:] = [o for _, o in locations]
-        packed[3 * n * 8:].view(np.int32)[:] = i64[:n] + 1
+        i64[2 * n:3 * n] = [o for _, o in locations]
+        i64[3 * n:] = i64[n:2 * n] * block_size + i64[2 * n:3 * n]
+        packed[4 * n * 8:].view(np.int32)[:] = i64[:n] + 1
         buf = torch.from_numpy(packed)
         if device.type == "cuda":
             buf = buf.pin_memory().to(device, non_blocking=True)
         self._packed, self.block_tables = buf, table
-        (self.positions, self.block_ids, self.offsets,
+        (self.positions, self.block_ids, self.offsets, self.slots,
          self.eff_seq_lens) = _unpack_meta(buf, n)
         self.public = self.snapshot()
 
@@ -74,14 +76,15 @@ class _DeviceMeta:
         """Fresh copies of the metadata (two copies: packed integers, table)."""
         pub = _unpack_meta(self._packed.clone(), len(self.positions))
         return dict(positions=pub[0], physical_block_ids=pub[1], block_offsets=pub[2],
-                    effective_seq_lens=pub[3], block_tables=self.block_tables.clone())
+                    effective_seq_lens=pub[4], block_tables=self.block_tables.clone())
 
 
 def _unpack_meta(buf, n):
-    """(positions, block ids, offsets) int64 and effective lengths int32 views
-    of a packed metadata buffer."""
-    i64 = buf[:3 * n * 8].view(torch.int64)
-    return i64[:n], i64[n:2 * n], i64[2 * n:], buf[3 * n * 8:].view(torch.int32)
+    """(positions, block ids, offsets, slots) int64 and effective lengths
+    int32 views of a packed metadata buffer."""
+    i64 = buf[:4 * n * 8].view(torch.int64)
+    return (i64[:n], i64[n:2 * n], i64[2 * n:3 * n], i64[3 * n:],
+            buf[4 * n * 8:].view(torch.int32))
 
 
 class _BlockTableCache:
@@ -128,12 +131,15 @@ class _BlockTableCache:
 class _FusedLayerLauncher:
     """Launch state of the engine's fused layer step for one open token.
 
-    Both C-ABI argument structs (``fd_rope_kv_append`` and ``fd_paged_decode``)
-    are filled once per transaction from the cache-owned device metadata and
-    the per-device decode workspace; a layer then only sets its q/k/v/output
-    pointers and the layer's cache planes.  The arithmetic is the same as the
-    checked path (same kernels, same arguments), only the host marshalling is
-    done once instead of per layer.
+    A layer is ONE ``fd_paged_decode`` launch with the fused append and RoPE
+    fields set: the kernel rotates q and the new K row by the transaction's
+    positions, stores the rotated K and the raw V row at the reserved slot
+    (``block_id * block_size + offset``) and attends over the sequence with
+    that row -- the same arithmetic as ``fd_rope_kv_append`` followed by
+    ``fd_paged_decode`` (one shared rotation routine; bit-identical caches and
+    outputs).  The argument struct is filled once per transaction from the
+    cache-owned device metadata and the per-device decode workspace; a layer
+    only sets its q/k/v/output pointers and the layer's cache planes.
     """
 
     def __init__(self, cache, meta, num_q_heads, sm_scale):
@@ -153,34 +159,13 @@ class _FusedLayerLauncher:
         self.v_layer_bytes = vc.stride(0) * esz
         q_strides = (num_q_heads * d, d, 1)
         kv_strides = (hkv * d, d, 1)
-
-        ra = _lib.RopeKVAppendArgs()
-        ra.struct_size = ctypes.sizeof(ra)
-        ra.dtype = _native.dtype_code(kc)
-        ra.batch = n
-        ra.num_q_heads = num_q_heads
-        ra.num_kv_heads = hkv
-        ra.head_dim = d
-        ra.block_size = bs
-        ra.num_blocks = cache.max_blocks
-        ra.q_stride[:] = q_strides
-        ra.q_out_stride[:] = q_strides
-        ra.k_stride[:] = kv_strides
-        ra.v_stride[:] = kv_strides
-        ra.k_cache_stride[:] = kc.stride()[1:]
-        ra.v_cache_stride[:] = vc.stride()[1:]
-        ra.block_ids = meta.block_ids.data_ptr()
-        ra.block_offsets = meta.offsets.data_ptr()
-        ra.positions = meta.positions.data_ptr()
-        ra.block_ids_index = ra.block_offsets_index = ra.positions_index = _lib.FD_INDEX_I64
-        self.ra = ra
         self.rope_key = None
         self.rope_args = None  # last (rotary_dim, base) as given, and its checked form
         self.rope_checked = None
 
         da = _lib.PagedDecodeArgs()
         da.struct_size = ctypes.sizeof(da)
-        da.dtype = ra.dtype
+        da.dtype = _native.dtype_code(kc)
         da.num_seqs = n
         da.num_q_heads = num_q_heads
         da.num_kv_heads = hkv
@@ -199,9 +184,17 @@ class _FusedLayerLauncher:
         da.seq_lens = meta.eff_seq_lens.data_ptr()
         da.seq_lens_index = _lib.FD_INDEX_I32
         da.seq_lens_stride = 1
+        da.append_k_stride[:] = kv_strides
+        da.append_v_stride[:] = kv_strides
+        da.slot_mapping = meta.slots.data_ptr()
+        da.slot_mapping_index = _lib.FD_INDEX_I64
+        da.slot_mapping_stride = 1
+        da.rope_positions = meta.positions.data_ptr()
+        da.rope_positions_index = _lib.FD_INDEX_I64
+        da.rope_positions_stride = 1
         da.epilogue = _lib.FD_EPILOGUE_FUSED
         # the plan (and so the workspace need) depends on shapes only
-        da.q = da.out = da.k_cache = da.v_cache = 1
+        da.q = da.out = da.k_cache = da.v_cache = da.append_k = da.append_v = 1
         scratch = ctypes.c_size_t(0)
         tickets = ctypes.c_int64(0)
         self.check(self.lib.fd_paged_decode_workspace(ctypes.byref(da), ctypes.byref(scratch),
@@ -221,12 +214,13 @@ class _FusedLayerLauncher:
     def _set_rope(self, rotary_dim, base):
         key = (rotary_dim, base)
         if key != self.rope_key:
-            self.ra.rotary_dim = rotary_dim
-            self.ra.inv_freq = _native.inv_freq_device(rotary_dim, base, self.device).data_ptr()
+            self.da.rope_dim = rotary_dim
+            self.da.rope_inv_freq = _native.inv_freq_device(rotary_dim, base,
+                                                            self.device).data_ptr()
             self.rope_key = key
 
     def run(self, layer_idx, q, k, v, rotary_dim, base):
-        """RoPE + K/V store, then decode; returns ``(q_rotated, output)``."""
+        """RoPE + K/V store + decode in one launch; returns the output."""
         if tuple(q.shape) != self.qshape or not q.is_contiguous():
             raise ValueError("q must be a contiguous [num_requests, num_q_heads, head_dim] tensor "
                              "matching the transaction")
@@ -235,19 +229,16 @@ class _FusedLayerLauncher:
             raise ValueError("k and v must be contiguous [num_requests, num_kv_heads, head_dim] "
                              "tensors matching the transaction")
         self._set_rope(rotary_dim, base)
-        # rotated q and output share one allocation (two contiguous halves)
-        buf = torch.empty((2,) + self.qshape, dtype=q.dtype, device=q.device)
-        q_rot, out = buf[0], buf[1]
-        stream = ctypes.c_void_p(_native.stream_handle(self.device))
-        ra, da = self.ra, self.da
-        kc = self.k_base + layer_idx * self.k_layer_bytes
-        vc = self.v_base + layer_idx * self.v_layer_bytes
-        ra.q, ra.q_out, ra.k, ra.v = q.data_ptr(), q_rot.data_ptr(), k.data_ptr(), v.data_ptr()
-        ra.k_cache, ra.v_cache = kc, vc
-        self.check(self.lib.fd_rope_kv_append(ctypes.byref(ra), stream), "fd_rope_kv_append")
-        da.q, da.out, da.k_cache, da.v_cache = q_rot.data_ptr(), out.data_ptr(), kc, vc
-        self.check(self.lib.fd_paged_decode(ctypes.byref(da), stream), "fd_paged_decode")
-        return q_rot, out
+        out = torch.empty(self.qshape, dtype=q.dtype, device=q.device)
+        da = self.da
+        da.q, da.out, da.append_k, da.append_v = (q.data_ptr(), out.data_ptr(), k.data_ptr(),
+                                                  v.data_ptr())
+        da.k_cache = self.k_base + layer_idx * self.k_layer_bytes
+        da.v_cache = self.v_base + layer_idx * self.v_layer_bytes
+        self.check(self.lib.fd_paged_decode(ctypes.byref(da),
+                                            ctypes.c_void_p(_native.stream_handle(self.device))),
+                   "fd_paged_decode")
+        return out
 
 
 class PagedKVCache:
@@ -414,7 +405,8 @@ class PagedKVCache:
         try:
             table = self._tables.get(self.device, ids,
                                      [self._ledger.requests[r].block_ids for r in ids])
-            tx.device_view = _DeviceMeta(self.device, tx.positions, tx.locations, table)
+            tx.device_view = _DeviceMeta(self.device, tx.positions, tx.locations, table,
+                                         self.block_size)
         except Exception:
             self._ledger.abort_token(tx)
             raise
@@ -473,9 +465,9 @@ class PagedKVCache:
                                              base=base, q_out=q_out)
 
     def _fused_layer_step(self, transaction, layer_idx, q, k, v, rotary_dim, base, sm_scale):
-        """Engine fast path of one layer: fused RoPE + K/V store at the
-        reserved slots, then paged decode over the transaction's block tables
-        and effective lengths.  Returns ``(q_rotated, output, public
+        """Engine fast path of one layer, one launch: RoPE of q and K, K/V
+        store at the reserved slots and paged decode over the transaction's
+        block tables and effective lengths.  Returns ``(output, public
         metadata)``; the launch arguments are prepared once per transaction
         (:class:`_FusedLayerLauncher`)."""
         # The engine has already checked q/k/v (tensors, shapes, device,
@@ -495,16 +487,16 @@ class PagedKVCache:
                 launcher.rope_checked = self._check_rope_args(rotary_dim, base)
                 launcher.rope_args = (rotary_dim, base)
             rotary_dim = launcher.rope_checked
-            if torch.cuda.current_device() != self.device.index:
+            if torch._C._cuda_getDevice() != self.device.index:
                 with torch.cuda.device(self.device):
-                    q_rot, out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
+                    out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
             else:
-                q_rot, out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
+                out = launcher.run(layer_idx, q, k, v, rotary_dim, float(base))
         except Exception:
             self._ledger.transaction_failure_count += 1
             raise
         self._ledger.record_layer_write(state, layer_idx)
-        return q_rot, out, meta.public
+        return out, meta.public
 
     def commit_token(self, transaction):
         """Publish one token after every layer has been written."""

@@ -57,6 +57,12 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kMaxRows = 16;  // query heads per head block (mma M)
 constexpr int kMaxStages = 16;
+// fused-append RoPE: inv_freq, then cos and sin of the current sequence's
+// angles (rope_dim / 2 <= 64 each)
+constexpr int kRopeFloats = 3 * 64;
+// fused-append row of the current segment: slot (int64) + K and V [2][128]
+// 16-bit values (the rotated K when RoPE is on)
+constexpr int kAppendInts = 2 + 128;
 constexpr int kMiscInts = 16;  // [0] abort, [1] ticket winner, [2] stream-K cut test,
                                // [8..9] cluster mbarrier
 constexpr float kLog2e = 1.4426950408889634f;
@@ -93,6 +99,13 @@ struct AttnParams {
   int slot64;
   int64_t slots;
   int fused_append;
+  // fused append with RoPE (rope_dim > 0): q rows and the appended K row are
+  // rotated by rope_pos[b] with the fp32 table rope_inv_freq[rope_dim / 2]
+  int rope_dim;
+  const float* rope_inv_freq;
+  const void* rope_pos;
+  int rope_pos64;
+  int64_t rope_pos_stride;
   int num_splits;  // 0 = length-balanced (stream-K) schedule
   int epilogue;    // FD_EPILOGUE_*
   int balanced;    // split mode: equal tile ranges instead of cdiv chunks
@@ -177,12 +190,12 @@ struct SeqInfo {
 // clamped to the block-table capacity so no read leaves the table row.
 __device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
   int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
+  // with a fused append the slot is read alongside the length (one round trip)
+  const int64_t slot =
+      p.fused_append ? load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) : 0;
   const int64_t cap = static_cast<int64_t>(p.max_blocks) * p.block_size;
   n = n < 0 ? 0 : (n > cap ? cap : n);
-  if (p.fused_append && n > 0) {
-    const int64_t s = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
-    if (s < 0) n = 0;
-  }
+  if (slot < 0) n = 0;
   SeqInfo r;
   r.n = static_cast<int>(n);
   r.tiles = static_cast<int>((n + kTile - 1) / kTile);
@@ -379,8 +392,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(mlbuf + kConsumerWarps * kMaxRows);
   uint64_t* empty_bar = full_bar + NST;
   uint32_t* stage_mask = reinterpret_cast<uint32_t*>(empty_bar + NST);
-  int* misc = reinterpret_cast<int*>(stage_mask + NST);  // [0] abort, [1] ticket winner
-  int* prefix = misc + kMiscInts;
+  // misc starts 16-byte aligned whatever the stage count: it holds the
+  // cluster mbarrier and the fused-append slot (8-byte objects)
+  int* misc = reinterpret_cast<int*>(
+      (reinterpret_cast<uintptr_t>(stage_mask + NST) + 15) & ~static_cast<uintptr_t>(15));
+  float* rope_tab = reinterpret_cast<float*>(misc + kMiscInts);  // [3][64]: inv_freq, cos, sin
+  int64_t* app_slot = reinterpret_cast<int64_t*>(misc + kMiscInts + kRopeFloats);
+  T* app_row = reinterpret_cast<T*>(app_slot + 1);  // [2][D]: K, V
+  int* prefix = misc + kMiscInts + kRopeFloats + kAppendInts;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -433,6 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0) prefix[0] = 0;
   }
+  // the RoPE table of the fused append, read once per CTA (its load overlaps
+  // the sequence-length loads above)
+  for (int i = tid; i < (p.rope_dim >> 1); i += kThreads) rope_tab[i] = p.rope_inv_freq[i];
   __syncthreads();
   if (streamk) {
     if (warp == 0) {  // chunked inclusive scan of prefix[1..num_seqs]
@@ -697,6 +719,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nr = min(p.rows, p.group - jb * p.rows);
     const T* qb = static_cast<const T*>(p.q) + b * p.qs0;
     uint8_t* qs = reinterpret_cast<uint8_t*>(obuf);
+    // RoPE position of this sequence (its load is in flight with q's)
+    const float posf =
+        p.rope_dim > 0 ? static_cast<float>(load_index(
+                             p.rope_pos, p.rope_pos64, static_cast<int64_t>(b) * p.rope_pos_stride))
+                       : 0.f;
+    // Fused append: this sequence's new K/V row and its slot are staged with
+    // q (same memory round trip), so the tile that receives the row reads
+    // shared memory only.  2 * D / 128 values per thread (1 or 2).
+    constexpr int kAppPer = (2 * D) / kConsumerThreads;
+    T app_v[kAppPer];
+    if (p.fused_append) {
+#pragma unroll
+      for (int j = 0; j < kAppPer; ++j) {
+        const int e = tid + j * kConsumerThreads;
+        const int plane = e / D;
+        const int d = e - plane * D;
+        app_v[j] = plane ? static_cast<const T*>(p.av)[b * p.avs0 + kvh * p.avs1 + d * p.avs2]
+                         : static_cast<const T*>(p.ak)[b * p.aks0 + kvh * p.aks1 + d * p.aks2];
+      }
+      if (tid == 0) *app_slot = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
+    }
     for (int c = tid; c < kMaxRows * (D / 8); c += kConsumerThreads) {
       const int row = c / (D / 8);
       const int ch = c - row * (D / 8);
@@ -714,7 +757,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       *reinterpret_cast<uint4*>(qs + chunk_offset(row, ch)) = v;
     }
+    if (p.fused_append) {
+#pragma unroll
+      for (int j = 0; j < kAppPer; ++j) app_row[tid + j * kConsumerThreads] = app_v[j];
+    }
+    if (tid < (p.rope_dim >> 1)) {
+      // cos / sin of this sequence's angles, once per pair index (the same
+      // for every q row and the K row)
+      float sn, cs;
+      sincosf(__fmul_rn(posf, rope_tab[tid]), &sn, &cs);
+      rope_tab[64 + tid] = cs;
+      rope_tab[128 + tid] = sn;
+    }
     named_barrier(kBarConsumers, kConsumerThreads);
+    if (p.rope_dim > 0) {
+      // RoPE in place of the staged q rows and (row nr) the appended K row:
+      // pair (i, i + rope_dim / 2)
+      const int half = p.rope_dim >> 1;
+      for (int e = tid; e < (nr + 1) * half; e += kConsumerThreads) {
+        const int row = e / half;
+        const int i = e - row * half;
+        T* x1p = row < nr ? reinterpret_cast<T*>(qs + tile_offset(row, i)) : app_row + i;
+        T* x2p = row < nr ? reinterpret_cast<T*>(qs + tile_offset(row, i + half))
+                          : app_row + i + half;
+        float y1, y2;
+        rope_rotate_pair_cs(to_f32<T>(*x1p), to_f32<T>(*x2p), rope_tab[64 + i], rope_tab[128 + i],
+                            y1, y2);
+        *x1p = from_f32<T>(y1);
+        *x2p = from_f32<T>(y2);
+      }
+      named_barrier(kBarConsumers, kConsumerThreads);
+    }
     const uint32_t qbase = smem_u32(qs);
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
@@ -795,20 +868,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         touched = true;
       }
       if (p.fused_append && (s.n - 1) >= base && (s.n - 1) < base + kTile) {
-        // current token: K/V come from the call; patch the tile and store the
-        // token into its cache slot (reference paged_decode.py:193-221).
+        // current token: K/V come from the call (staged with q, K rotated
+        // when RoPE is on); patch the tile and store the token into its cache
+        // slot (reference paged_decode.py:193-221).
         const int ra = s.n - 1 - base;
-        const T* akp = static_cast<const T*>(p.ak) + s.b * p.aks0 + kv_head * p.aks1;
-        const T* avp = static_cast<const T*>(p.av) + s.b * p.avs0 + kv_head * p.avs1;
-        const int64_t slot = load_index(p.slot, p.slot64, static_cast<int64_t>(s.b) * p.slots);
+        const int64_t slot = *app_slot;
         const int64_t sblk = slot >> bs_shift;
         const int64_t soff = slot - sblk * bs;
         const bool store = (jblk == 0) && sblk < p.num_blocks;
         T* kc = static_cast<T*>(p.k) + sblk * p.ks0 + kv_head * p.ks1 + soff * p.ks2;
         T* vc = static_cast<T*>(p.v) + sblk * p.vs0 + kv_head * p.vs1 + soff * p.vs2;
         for (int d = lane; d < D; d += 32) {
-          const T kv = akp[d * p.aks2];
-          const T vv = avp[d * p.avs2];
+          const T kv = app_row[d];
+          const T vv = app_row[D + d];
           *reinterpret_cast<T*>(sb + stage_tile_offset<kPageRows>(ra, d)) = kv;
           *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes +
                                 stage_tile_offset<kPageRows>(ra, d)) = vv;
@@ -1225,7 +1297,8 @@ template <int D>
 size_t smem_bytes(int stages, int sched_ints) {
   using SM = Smem<D>;
   return 1024 + static_cast<size_t>(stages) * SM::kStageBytes + SM::kMergeBytes +
-         static_cast<size_t>(stages) * 20 + (kMiscInts + sched_ints) * sizeof(int);
+         static_cast<size_t>(stages) * 20 + 16 +
+         (kMiscInts + kRopeFloats + kAppendInts + sched_ints) * sizeof(int);
 }
 
 struct Derived {
@@ -1254,6 +1327,12 @@ int validate(const fd_paged_decode_args* a) {
   if (!a->q || !a->out || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens)
     return FD_ERR_INVALID_ARGUMENT;
   if (a->append_k && (!a->append_v || !a->slot_mapping)) return FD_ERR_INVALID_ARGUMENT;
+  if (a->rope_dim != 0) {
+    // RoPE applies to the fused-append row: q and the appended K
+    if (!a->append_k || a->rope_dim < 0 || (a->rope_dim & 1) || a->rope_dim > a->head_dim ||
+        !a->rope_inv_freq || !a->rope_positions)
+      return FD_ERR_INVALID_ARGUMENT;
+  }
   if (a->num_splits < 0 || a->num_splits > 4096) return FD_ERR_INVALID_ARGUMENT;
   if (a->epilogue != FD_EPILOGUE_FUSED && a->epilogue != FD_EPILOGUE_PARTIALS)
     return FD_ERR_INVALID_ARGUMENT;
@@ -1531,6 +1610,13 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
     p.slot = a->slot_mapping;
     p.slot64 = a->slot_mapping_index == FD_INDEX_I64;
     p.slots = a->slot_mapping_stride;
+    p.rope_dim = a->rope_dim;
+    if (a->rope_dim > 0) {
+      p.rope_inv_freq = a->rope_inv_freq;
+      p.rope_pos = a->rope_positions;
+      p.rope_pos64 = a->rope_positions_index == FD_INDEX_I64;
+      p.rope_pos_stride = a->rope_positions_stride;
+    }
   }
   p.num_splits = plan.splits;
   p.balanced = plan.balanced;

@@ -205,6 +205,26 @@ __device__ __forceinline__ float from_f32<float>(float v) {
   return v;
 }
 
+// Split-half RoPE of one dimension pair (flashdec/rope.py:66-79):
+//   y1 = x1 cos(a) - x2 sin(a),  y2 = x2 cos(a) + x1 sin(a),  a = pos * inv_freq
+// in fp32 with every product and sum rounded separately (torch's evaluation
+// of `x1 * cos - x2 * sin`, no FMA contraction) and the accurate sincosf.
+// Both the RoPE + append kernel and the decode kernel's fused append use
+// these routines (the decode kernel computes each pair index's cos/sin once
+// per sequence with the same expression), so their rotated values are
+// bit-identical.
+__device__ __forceinline__ void rope_rotate_pair_cs(float x1, float x2, float cs, float sn,
+                                                    float& y1, float& y2) {
+  y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+  y2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+}
+__device__ __forceinline__ void rope_rotate_pair(float x1, float x2, float posf, float inv_freq,
+                                                 float& y1, float& y2) {
+  float sn, cs;
+  sincosf(__fmul_rn(posf, inv_freq), &sn, &cs);
+  rope_rotate_pair_cs(x1, x2, cs, sn, y1, y2);
+}
+
 // Load one integer element (int32 or int64 storage) as int64.
 __device__ __forceinline__ int64_t load_index(const void* base, int is64, int64_t i) {
   return is64 ? static_cast<const int64_t*>(base)[i]

@@ -54,13 +54,11 @@ __device__ __forceinline__ void rotate_row(const T* x, int64_t xs, T* y, int64_t
                                            int lane) {
   const int half = rotary_dim >> 1;
   for (int i = lane; i < half; i += 32) {
-    const float x1 = to_f32<T>(x[i * xs]);
-    const float x2 = to_f32<T>(x[(i + half) * xs]);
-    const float ang = __fmul_rn(posf, inv_freq[i]);
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
-    y[i * ys] = from_f32<T>(__fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn)));
-    y[(i + half) * ys] = from_f32<T>(__fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn)));
+    float y1, y2;
+    rope_rotate_pair(to_f32<T>(x[i * xs]), to_f32<T>(x[(i + half) * xs]), posf, inv_freq[i], y1,
+                     y2);
+    y[i * ys] = from_f32<T>(y1);
+    y[(i + half) * ys] = from_f32<T>(y2);
   }
   for (int i = rotary_dim + lane; i < head_dim; i += 32) y[i * ys] = x[i * xs];
 }

@@ -13,11 +13,14 @@ plus the single-layer ``step`` wrapper (engine.py:754-871), ``metrics`` and
 ``validate_invariants``, with the reference's dataclasses, state names,
 validation order and error messages.
 
-Each layer is two launches on the caller's stream: ``fd_rope_kv_append``
-(RoPE of Q and K, K/V stored at the slots reserved by ``begin_step``) and
-``fd_paged_decode`` over the transaction's block tables and effective
-lengths.  The transaction metadata is uploaded once per token by the cache and
-read by every layer; nothing in a layer synchronises with the device.
+With ``append_backend='fused_cuda'`` each layer is ONE launch on the
+caller's stream: ``fd_paged_decode`` with its fused-append and RoPE fields,
+which rotates q and the new K row, stores K/V at the slots reserved by
+``begin_step`` and attends over the transaction's block tables and effective
+lengths.  The other append backends run ``fd_rope_kv_append`` and then
+``fd_paged_decode`` (two launches; same arithmetic).  The transaction
+metadata is uploaded once per token by the cache and read by every layer;
+nothing in a layer synchronises with the device.
 
 Differences from the reference, by design:
 
@@ -291,10 +294,10 @@ class DecodeEngine:
             if v.dim() == 2:
                 v = v.unsqueeze(0)
             if self.append_backend == "fused_cuda" and self._range is None:
-                # one prepared launch pair per layer (same kernels and
-                # arguments as the checked path below)
-                _, out, pub = self.cache._fused_layer_step(st.cache_tx, layer_idx, q, k, v,
-                                                           rotary_dim, base, self.sm_scale)
+                # one prepared launch per layer: RoPE + K/V store + decode
+                # (same arithmetic as the checked two-launch path below)
+                out, pub = self.cache._fused_layer_step(st.cache_tx, layer_idx, q, k, v,
+                                                        rotary_dim, base, self.sm_scale)
                 st.next_layer_idx += 1
                 st.last_output = out
                 self._transaction_layer_step_count += 1
@@ -337,7 +340,11 @@ class DecodeEngine:
         return DecodeStepResult(
             status=self.STEP_OK, request_ids=st.handle.request_ids, output=st.last_output,
             positions=committed.positions, block_tables=committed.block_tables,
-            seq_lens=self.cache.seq_lens_tensor(st.handle.request_ids),
+            # the committed lengths are the transaction's effective lengths
+            # (position + 1); copying the device tensor keeps the host from
+            # waiting for the step's kernels (a host-built tensor would be a
+            # blocking upload behind them)
+            seq_lens=st.handle.effective_seq_lens.clone(),
             needed_new_blocks=st.needed_new_blocks, free_blocks=self.cache.num_free_blocks)
 
     def abort_step(self, transaction):

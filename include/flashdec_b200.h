@@ -131,6 +131,19 @@ typedef struct fd_paged_decode_args {
   size_t scratch_bytes;
   int32_t max_ctas;          /* 0: one CTA per SM */
   int32_t min_tiles_per_cta; /* 0: default (4); auto schedule only */
+
+  /* optional split-half RoPE of the fused-append row (needs append_k; 0: off).
+   * q[s] and append_k[s] are rotated by position rope_positions[s] with the
+   * fp32 table rope_inv_freq[rope_dim / 2] (= base^(-2i/rope_dim), computed
+   * like flashdec/rope.py:66-67), exactly as fd_rope_kv_append rotates them;
+   * the rotated K row is what the cache slot receives.  One launch then does
+   * a whole decode layer of flashdec/engine.py:1072-1183 (RoPE + K/V store
+   * + paged attention). */
+  int32_t rope_dim;
+  const float* rope_inv_freq;
+  const void* rope_positions;
+  int32_t rope_positions_index;
+  int64_t rope_positions_stride;
 } fd_paged_decode_args;
 
 /* Workspace needed by fd_paged_decode for `args`: scratch bytes and ticket
