@@ -57,9 +57,9 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kMaxRows = 16;  // query heads per head block (mma M)
 constexpr int kMaxStages = 16;
-// fused-append RoPE: inv_freq, then cos and sin of the current sequence's
-// angles (rope_dim / 2 <= 64 each)
-constexpr int kRopeFloats = 3 * 64;
+// fused-append RoPE: cos and sin of the current sequence's angles
+// (rope_dim / 2 <= 64 each)
+constexpr int kRopeFloats = 2 * 64;
 // fused-append row of the current segment: slot (int64) + K and V [2][128]
 // 16-bit values (the rotated K when RoPE is on)
 constexpr int kAppendInts = 2 + 128;
@@ -188,14 +188,16 @@ struct SeqInfo {
 // Reference semantics (paged_decode.py:263-264, :398-403): the sequence is
 // active when seq_len > 0 and, with a fused append, slot >= 0.  seq_len is
 // clamped to the block-table capacity so no read leaves the table row.
+template <bool kAppend>
 __device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
   int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
-  // with a fused append the slot is read alongside the length (one round trip)
-  const int64_t slot =
-      p.fused_append ? load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) : 0;
   const int64_t cap = static_cast<int64_t>(p.max_blocks) * p.block_size;
   n = n < 0 ? 0 : (n > cap ? cap : n);
-  if (slot < 0) n = 0;
+  if constexpr (kAppend) {
+    // the slot is read alongside the length (one memory round trip)
+    const int64_t slot = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
+    if (slot < 0) n = 0;
+  }
   SeqInfo r;
   r.n = static_cast<int>(n);
   r.tiles = static_cast<int>((n + kTile - 1) / kTile);
@@ -280,6 +282,7 @@ __device__ __forceinline__ void split_range(const AttnParams& p, int split, int 
   }
 }
 
+template <bool kAppend>
 __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Segment& s) {
   if (p.num_splits == 0) {
     if (sc.x >= sc.hi) return false;
@@ -310,7 +313,7 @@ __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Seg
   const int split = static_cast<int>(blockIdx.x);
   s.hb = static_cast<int>(blockIdx.y);
   s.b = static_cast<int>(blockIdx.z);
-  const SeqInfo si = seq_info(p, s.b);
+  const SeqInfo si = seq_info<kAppend>(p, s.b);
   s.n = si.n;
   s.tiles = si.tiles;
   split_range(p, split, si.tiles, s.t0, s.t1);
@@ -376,7 +379,7 @@ __device__ __forceinline__ int tmap_coord(int axis, int kv_head, int blk) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <typename T, int D, bool kTma, int kPageRows>
+template <typename T, int D, bool kTma, int kPageRows, bool kAppend>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ AttnParams p,
                         const __grid_constant__ CUtensorMap tmap_k,
@@ -396,10 +399,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // cluster mbarrier and the fused-append slot (8-byte objects)
   int* misc = reinterpret_cast<int*>(
       (reinterpret_cast<uintptr_t>(stage_mask + NST) + 15) & ~static_cast<uintptr_t>(15));
-  float* rope_tab = reinterpret_cast<float*>(misc + kMiscInts);  // [3][64]: inv_freq, cos, sin
+  float* rope_tab = reinterpret_cast<float*>(misc + kMiscInts);  // [2][64]: cos, sin
   int64_t* app_slot = reinterpret_cast<int64_t*>(misc + kMiscInts + kRopeFloats);
   T* app_row = reinterpret_cast<T*>(app_slot + 1);  // [2][D]: K, V
-  int* prefix = misc + kMiscInts + kRopeFloats + kAppendInts;
+  // the RoPE table and the append row exist only for a fused append (the
+  // other calls keep that shared memory for the stage ring)
+  int* prefix = misc + kMiscInts + (kAppend ? kRopeFloats + kAppendInts : 0);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -446,15 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool streamk = (p.num_splits == 0);
   if (streamk) {
     for (int b = tid; b < p.num_seqs; b += kThreads) {
-      const SeqInfo si = seq_info(p, b);
+      const SeqInfo si = seq_info<kAppend>(p, b);
       prefix[b + 1] = si.tiles;
       seqn[b] = si.n;
     }
     if (tid == 0) prefix[0] = 0;
   }
-  // the RoPE table of the fused append, read once per CTA (its load overlaps
-  // the sequence-length loads above)
-  for (int i = tid; i < (p.rope_dim >> 1); i += kThreads) rope_tab[i] = p.rope_inv_freq[i];
   __syncthreads();
   if (streamk) {
     if (warp == 0) {  // chunked inclusive scan of prefix[1..num_seqs]
@@ -569,10 +571,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       win_next = bt_entry(win_b, wb + 32 + lane);
     }
     Segment s;
-    while (next_segment(p, sc, s)) {
+    while (next_segment<kAppend>(p, sc, s)) {
       if (s.t1 <= s.t0) continue;
       const int kv_head = s.hb / p.hb_per_kv;
-      const int limit_cache = p.fused_append ? s.n - 1 : s.n;  // tokens read from the cache
+      const int limit_cache = kAppend ? s.n - 1 : s.n;  // tokens read from the cache
       const int64_t nlb = (limit_cache + bs - 1) >> bs_shift;  // pages holding them
       for (int tg = s.t0; tg < s.t1;) {
         const int64_t pg0 = static_cast<int64_t>(tg) << ppt_shift;
@@ -720,16 +722,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const T* qb = static_cast<const T*>(p.q) + b * p.qs0;
     uint8_t* qs = reinterpret_cast<uint8_t*>(obuf);
     // RoPE position of this sequence (its load is in flight with q's)
+    const bool rope_pair = kAppend && tid < (p.rope_dim >> 1);
     const float posf =
-        p.rope_dim > 0 ? static_cast<float>(load_index(
-                             p.rope_pos, p.rope_pos64, static_cast<int64_t>(b) * p.rope_pos_stride))
-                       : 0.f;
+        rope_pair ? static_cast<float>(load_index(p.rope_pos, p.rope_pos64,
+                                                  static_cast<int64_t>(b) * p.rope_pos_stride))
+                  : 0.f;
+    const float invf = rope_pair ? p.rope_inv_freq[tid] : 0.f;
     // Fused append: this sequence's new K/V row and its slot are staged with
     // q (same memory round trip), so the tile that receives the row reads
     // shared memory only.  2 * D / 128 values per thread (1 or 2).
     constexpr int kAppPer = (2 * D) / kConsumerThreads;
     T app_v[kAppPer];
-    if (p.fused_append) {
+    if (kAppend) {
 #pragma unroll
       for (int j = 0; j < kAppPer; ++j) {
         const int e = tid + j * kConsumerThreads;
@@ -757,20 +761,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       *reinterpret_cast<uint4*>(qs + chunk_offset(row, ch)) = v;
     }
-    if (p.fused_append) {
+    if (kAppend) {
 #pragma unroll
       for (int j = 0; j < kAppPer; ++j) app_row[tid + j * kConsumerThreads] = app_v[j];
     }
-    if (tid < (p.rope_dim >> 1)) {
+    if (rope_pair) {
       // cos / sin of this sequence's angles, once per pair index (the same
       // for every q row and the K row)
       float sn, cs;
-      sincosf(__fmul_rn(posf, rope_tab[tid]), &sn, &cs);
-      rope_tab[64 + tid] = cs;
-      rope_tab[128 + tid] = sn;
+      sincosf(__fmul_rn(posf, invf), &sn, &cs);
+      rope_tab[tid] = cs;
+      rope_tab[64 + tid] = sn;
     }
     named_barrier(kBarConsumers, kConsumerThreads);
-    if (p.rope_dim > 0) {
+    if (kAppend && p.rope_dim > 0) {
       // RoPE in place of the staged q rows and (row nr) the appended K row:
       // pair (i, i + rope_dim / 2)
       const int half = p.rope_dim >> 1;
@@ -781,8 +785,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         T* x2p = row < nr ? reinterpret_cast<T*>(qs + tile_offset(row, i + half))
                           : app_row + i + half;
         float y1, y2;
-        rope_rotate_pair_cs(to_f32<T>(*x1p), to_f32<T>(*x2p), rope_tab[64 + i], rope_tab[128 + i],
-                            y1, y2);
+        rope_rotate_pair_cs(to_f32<T>(*x1p), to_f32<T>(*x2p), rope_tab[i], rope_tab[64 + i], y1,
+                            y2);
         *x1p = from_f32<T>(y1);
         *x2p = from_f32<T>(y2);
       }
@@ -815,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   Segment s;
-  while (next_segment(p, sc, s)) {
+  while (next_segment<kAppend>(p, sc, s)) {
     const int kv_head = s.hb / p.hb_per_kv;
     const int jblk = s.hb % p.hb_per_kv;
     const int head0 = kv_head * p.group + jblk * p.rows;
@@ -827,7 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
-    const int limit_cache = p.fused_append ? s.n - 1 : s.n;
+    const int limit_cache = kAppend ? s.n - 1 : s.n;
     for (int t = s.t0; t < s.t1; ++t) {
       const int stage = cst;
       const uint32_t phase = cph;
@@ -849,7 +853,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // valid rows of this tile
       const int pos = base + lane;
       const bool from_cache = pos < limit_cache && ((pmask >> (lane >> bs_shift)) & 1u);
-      const bool appended = p.fused_append && pos == s.n - 1;
+      const bool appended = kAppend && pos == s.n - 1;
       const uint32_t vmask = __ballot_sync(0xffffffffu, from_cache || appended);
       bool touched = false;
       if (vmask != 0xffffffffu) {
@@ -867,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         touched = true;
       }
-      if (p.fused_append && (s.n - 1) >= base && (s.n - 1) < base + kTile) {
+      if (kAppend && (s.n - 1) >= base && (s.n - 1) < base + kTile) {
         // current token: K/V come from the call (staged with q, K rotated
         // when RoPE is on); patch the tile and store the token into its cache
         // slot (reference paged_decode.py:193-221).
@@ -1294,11 +1298,11 @@ __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
 namespace {
 
 template <int D>
-size_t smem_bytes(int stages, int sched_ints) {
+size_t smem_bytes(int stages, int sched_ints, bool fused_append) {
   using SM = Smem<D>;
   return 1024 + static_cast<size_t>(stages) * SM::kStageBytes + SM::kMergeBytes +
          static_cast<size_t>(stages) * 20 + 16 +
-         (kMiscInts + kRopeFloats + kAppendInts + sched_ints) * sizeof(int);
+         (kMiscInts + (fused_append ? kRopeFloats + kAppendInts : 0) + sched_ints) * sizeof(int);
 }
 
 struct Derived {
@@ -1455,10 +1459,10 @@ int max_active_clusters(K kern, size_t smem, int size, const DeviceInfo& dev) {
   return n;
 }
 
-template <typename T, int D, bool kTma, int kPageRows>
+template <typename T, int D, bool kTma, int kPageRows, bool kAppend>
 int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
            size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
-  auto kern = paged_decode_kernel<T, D, kTma, kPageRows>;
+  auto kern = paged_decode_kernel<T, D, kTma, kPageRows, kAppend>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   const int slot = dev.device & 63;
@@ -1506,18 +1510,28 @@ int launch(AttnParams prm, const CUtensorMap& mk, const CUtensorMap& mv, dim3 gr
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm, mk, mv));
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kAppend>
 int dispatch_tma(bool tma, const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
                  dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
-  if (!tma) return launch<T, D, false, 0>(prm, mk, mv, grid, smem, dev, st);
+  if (!tma) return launch<T, D, false, 0, kAppend>(prm, mk, mv, grid, smem, dev, st);
   if constexpr (D == 128) {
     // whole-plane boxes (5-D maps) for 16- and 8-token pages
     if (prm.kperm[3] >= 0) {
-      return prm.block_size == 16 ? launch<T, D, true, 16>(prm, mk, mv, grid, smem, dev, st)
-                                  : launch<T, D, true, 8>(prm, mk, mv, grid, smem, dev, st);
+      return prm.block_size == 16
+                 ? launch<T, D, true, 16, kAppend>(prm, mk, mv, grid, smem, dev, st)
+                 : launch<T, D, true, 8, kAppend>(prm, mk, mv, grid, smem, dev, st);
     }
   }
-  return launch<T, D, true, 0>(prm, mk, mv, grid, smem, dev, st);
+  return launch<T, D, true, 0, kAppend>(prm, mk, mv, grid, smem, dev, st);
+}
+
+// The fused-append variant (current token from the call, optional RoPE) is a
+// separate instantiation, so the plain decode carries none of its code.
+template <typename T, int D>
+int dispatch(bool tma, const AttnParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
+             dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
+  return prm.fused_append ? dispatch_tma<T, D, true>(tma, prm, mk, mv, grid, smem, dev, st)
+                          : dispatch_tma<T, D, false>(tma, prm, mk, mv, grid, smem, dev, st);
 }
 
 }  // namespace
@@ -1686,7 +1700,13 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
   if (plan.splits == 0 &&
       static_cast<int64_t>(a->num_seqs) * dv.nhb * plan.cap_tiles >= (int64_t(1) << 31))
     return FD_ERR_UNSUPPORTED;
-  const size_t fixed = (D == 128 ? smem_bytes<128>(0, sched_ints) : smem_bytes<64>(0, sched_ints));
+  // The stage count is sized as if the fused-append area were present, for
+  // both variants: tile t is consumed by warp (t mod stages) mod 4, so equal
+  // stage counts give the plain and the fused-append launch the same
+  // per-warp summation order (bit-identical results for the same tiles).
+  const bool fa = p.fused_append != 0;
+  const size_t fixed =
+      (D == 128 ? smem_bytes<128>(0, sched_ints, true) : smem_bytes<64>(0, sched_ints, true));
   const size_t stage_bytes = (D == 128 ? Smem<128>::kStageBytes : Smem<64>::kStageBytes) + 20;
   const size_t cap = static_cast<size_t>(dev->max_smem_optin);
   if (fixed + 2 * stage_bytes > cap) return FD_ERR_UNSUPPORTED;  // batch too large for the schedule
@@ -1698,15 +1718,16 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
   // ahead, for any stage count of at least four.
   if (stages < kConsumerWarps) return FD_ERR_UNSUPPORTED;
   p.num_stages = stages;
-  const size_t smem = D == 128 ? smem_bytes<128>(stages, sched_ints) : smem_bytes<64>(stages, sched_ints);
+  const size_t smem = D == 128 ? smem_bytes<128>(stages, sched_ints, fa)
+                                : smem_bytes<64>(stages, sched_ints, fa);
 
   const bool bf16 = a->dtype == FD_DTYPE_BF16;
   if (D == 128) {
-    return bf16 ? dispatch_tma<__nv_bfloat16, 128>(tma, p, mk, mv, gdim, smem, *dev, stream)
-                : dispatch_tma<__half, 128>(tma, p, mk, mv, gdim, smem, *dev, stream);
+    return bf16 ? dispatch<__nv_bfloat16, 128>(tma, p, mk, mv, gdim, smem, *dev, stream)
+                : dispatch<__half, 128>(tma, p, mk, mv, gdim, smem, *dev, stream);
   }
-  return bf16 ? dispatch_tma<__nv_bfloat16, 64>(tma, p, mk, mv, gdim, smem, *dev, stream)
-              : dispatch_tma<__half, 64>(tma, p, mk, mv, gdim, smem, *dev, stream);
+  return bf16 ? dispatch<__nv_bfloat16, 64>(tma, p, mk, mv, gdim, smem, *dev, stream)
+              : dispatch<__half, 64>(tma, p, mk, mv, gdim, smem, *dev, stream);
 }
 
 extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_stream) {
