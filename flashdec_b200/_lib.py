@@ -58,6 +58,15 @@ class PagedDecodeArgs(ctypes.Structure):
     ]
 
 
+class CascadeArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", _i32), ("num_groups", _i32), ("group_start", _vp),
+        ("group_members", _vp), ("group_pages", _vp), ("seq_prefix_pages", _vp),
+        ("max_group_members", _i32), ("max_prefix_tiles", _i32), ("chunks", _i32),
+        ("tail_splits", _i32),
+    ]
+
+
 class SplitReduceArgs(ctypes.Structure):
     _fields_ = [
         ("struct_size", _i32), ("dtype", _i32), ("num_seqs", _i32), ("num_q_heads", _i32),
@@ -89,7 +98,7 @@ class RopeKVAppendArgs(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "fd_paged_decode_workspace", "fd_paged_decode", "fd_split_kv_reduce", "fd_rope_kv_append",
     "fd_error_string", "fd_version", "fd_device_status", "fd_num_sms", "fd_paged_decode_static",
-    "fd_selftest_wait_timeout",
+    "fd_selftest_wait_timeout", "fd_cascade_workspace", "fd_cascade_decode",
 )
 
 _lock = threading.Lock()
@@ -124,6 +133,11 @@ def load_library():
         lib.fd_paged_decode.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp]
         lib.fd_paged_decode_static.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp]
         lib.fd_split_kv_reduce.argtypes = [ctypes.POINTER(SplitReduceArgs), _vp]
+        lib.fd_cascade_workspace.argtypes = [ctypes.POINTER(PagedDecodeArgs),
+                                             ctypes.POINTER(CascadeArgs),
+                                             ctypes.POINTER(ctypes.c_size_t)]
+        lib.fd_cascade_decode.argtypes = [ctypes.POINTER(PagedDecodeArgs),
+                                          ctypes.POINTER(CascadeArgs), _vp]
         lib.fd_rope_kv_append.argtypes = [ctypes.POINTER(RopeKVAppendArgs), _vp]
         lib.fd_error_string.argtypes = [ctypes.c_int]
         lib.fd_error_string.restype = ctypes.c_char_p

@@ -224,6 +224,75 @@ def paged_decode(q, k4, v4, block_tables, seq_lens, out, **kw):
     return out
 
 
+class CascadeGroups:
+    """Device description of the shared-prefix groups of a batch for
+    ``fd_cascade_decode``: ``groups`` lists the sequence indices (rows of q)
+    of each group and ``pages`` its shared leading pages (the same physical
+    pages at the start of every member's block-table row; ``pages *
+    block_size`` a multiple of 32)."""
+
+    def __init__(self, groups, pages, num_seqs, block_size, device):
+        if len(groups) != len(pages) or not groups:
+            raise ValueError("one page count per group, at least one group")
+        start = [0]
+        members = []
+        seq_pages = [0] * int(num_seqs)
+        for g, pg in zip(groups, pages):
+            if (int(pg) * int(block_size)) % 32:
+                raise ValueError("shared prefix tokens must be a multiple of 32")
+            for b in g:
+                if not 0 <= int(b) < num_seqs or seq_pages[int(b)]:
+                    raise ValueError("group members must be distinct rows of the batch")
+                seq_pages[int(b)] = int(pg)
+            members += [int(b) for b in g]
+            start.append(len(members))
+        host = torch.tensor(start + members + [int(x) for x in pages] + seq_pages,
+                            dtype=torch.int32)
+        self.data = host.pin_memory().to(device, non_blocking=True) \
+            if torch.device(device).type == "cuda" else host
+        ng, nm = len(groups), len(members)
+        self.args = _lib.CascadeArgs()
+        a = self.args
+        a.struct_size = ctypes.sizeof(_lib.CascadeArgs)
+        a.num_groups = ng
+        base, esz = self.data.data_ptr(), 4
+        a.group_start = base
+        a.group_members = base + (ng + 1) * esz
+        a.group_pages = base + (ng + 1 + nm) * esz
+        a.seq_prefix_pages = base + (ng + 1 + nm + ng) * esz
+        a.max_group_members = max(len(g) for g in groups)
+        a.max_prefix_tiles = max(int(pg) * int(block_size) // 32 for pg in pages)
+
+
+def cascade_workspace_bytes(decode_args, cascade_args):
+    lib = _lib.load_library()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.fd_cascade_workspace(ctypes.byref(decode_args), ctypes.byref(cascade_args),
+                                        ctypes.byref(nbytes)), "fd_cascade_workspace")
+    return nbytes.value
+
+
+def cascade_decode(q, k4, v4, block_tables, seq_lens, out, groups, *, sm_scale, block_size,
+                   num_seqs, chunks=0, tail_splits=0, append_k=None, append_v=None,
+                   slot_mapping=None, rope=None):
+    """Launch ``fd_cascade_decode`` (prefix pass, tail pass, merge) on the
+    current stream; ``groups`` is a :class:`CascadeGroups`.  Returns ``out``."""
+    prep = prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, sm_scale=sm_scale,
+                                block_size=block_size, num_seqs=num_seqs, num_splits=1,
+                                append_k=append_k, append_v=append_v,
+                                slot_mapping=slot_mapping, rope=rope)
+    a = prep.args
+    c = groups.args
+    c.chunks, c.tail_splits = int(chunks), int(tail_splits)
+    nbytes = cascade_workspace_bytes(a, c)
+    _, scratch = workspace(q.device, 0, nbytes)
+    a.scratch, a.scratch_bytes = scratch.data_ptr(), scratch.numel() * 4
+    _lib.check(prep.lib.fd_cascade_decode(ctypes.byref(a), ctypes.byref(c),
+                                          ctypes.c_void_p(stream_handle(q.device))),
+               "fd_cascade_decode")
+    return out
+
+
 def split_kv_reduce(acc, mx, sm, seq_lens, out, *, num_seqs, slot_mapping=None):
     lib = _lib.load_library()
     a = _lib.SplitReduceArgs()

@@ -106,6 +106,9 @@ struct AttnParams {
   const void* rope_pos;
   int rope_pos64;
   int64_t rope_pos_stride;
+  // cascade tail pass: sequence b attends only to its tokens after its first
+  // pre_pages[b] pages (a shared prefix handled by the prefix pass)
+  const int* pre_pages;
   int num_splits;  // 0 = length-balanced (stream-K) schedule
   int epilogue;    // FD_EPILOGUE_*
   int balanced;    // split mode: equal tile ranges instead of cdiv chunks
@@ -183,6 +186,7 @@ __device__ __forceinline__ uint32_t chunk_offset(int row, int chunk) {
 struct SeqInfo {
   int n;      // tokens attended (0 => nothing to attend: zero output)
   int tiles;  // cdiv(n, 32)
+  int off;    // pages skipped at the start of the block-table row (cascade tail)
 };
 
 // Reference semantics (paged_decode.py:263-264, :398-403): the sequence is
@@ -199,6 +203,14 @@ __device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
     if (slot < 0) n = 0;
   }
   SeqInfo r;
+  r.off = 0;
+  if (p.pre_pages) {
+    // cascade tail: the first pre_pages[b] pages are attended by the prefix pass
+    const int off = min(max(p.pre_pages[b], 0), p.max_blocks);
+    const int64_t skip = static_cast<int64_t>(off) * p.block_size;
+    n = n > skip ? n - skip : 0;
+    r.off = off;
+  }
   r.n = static_cast<int>(n);
   r.tiles = static_cast<int>((n + kTile - 1) / kTile);
   return r;
@@ -207,6 +219,7 @@ __device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
 // A piece of work: tiles [t0, t1) of pair (b, hb).
 struct Segment {
   int b, hb, t0, t1, n, tiles;
+  int off;        // block-table pages before tile 0 (cascade tail pass)
   int whole;      // covers the whole pair: write the output directly
   int part_slot;  // stream-K slot id or split index
   int nseg;       // contributors to the pair's ticket
@@ -303,6 +316,7 @@ __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Seg
     s.nseg = sc.owner(pair_end - 1) - s.c_first + 1;
     s.part_slot = static_cast<int>(blockIdx.x) + b * p.nhb + hb;
     s.n = sc.seqn[b];
+    s.off = 0;  // (the cascade tail pass runs the split schedule)
     sc.x = seg_end;
     return true;
   }
@@ -315,6 +329,7 @@ __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Seg
   s.b = static_cast<int>(blockIdx.z);
   const SeqInfo si = seq_info<kAppend>(p, s.b);
   s.n = si.n;
+  s.off = si.off;
   s.tiles = si.tiles;
   split_range(p, split, si.tiles, s.t0, s.t1);
   s.whole = (S == 1) && p.epilogue == FD_EPILOGUE_FUSED;
@@ -553,13 +568,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // page wb + 32 + l (win_next, prefetched); win_b is the sequence.
     int64_t wb = -1;
     int win_b = -1, win = -1, win_next = -1;
+    int seg_off = 0;  // the current segment's leading pages (cascade tail)
     auto bt_entry = [&](int b, int64_t lb) -> int {
+      lb += seg_off;
       return lb < p.max_blocks
                  ? static_cast<int>(load_index(p.bt, p.bt64,
                                                static_cast<int64_t>(b) * p.bts0 + lb * p.bts1))
                  : -1;
     };
-    if (!streamk) {
+    if (!streamk && !p.pre_pages) {
       // Split schedule: this CTA's pair and (for a full-length sequence) its
       // pages are known from blockIdx alone, so the first window is fetched
       // speculatively, in parallel with the sequence-length load.
@@ -573,6 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Segment s;
     while (next_segment<kAppend>(p, sc, s)) {
       if (s.t1 <= s.t0) continue;
+      seg_off = s.off;  // fixed per sequence, so a window of this sequence stays valid
       const int kv_head = s.hb / p.hb_per_kv;
       const int limit_cache = kAppend ? s.n - 1 : s.n;  // tokens read from the cache
       const int64_t nlb = (limit_cache + bs - 1) >> bs_shift;  // pages holding them
@@ -1258,6 +1276,10 @@ struct ReduceParams {
   int64_t slots;
   void* out;
   int64_t os0, os1, os2;
+  // cascade: sequences with pre_pages[b] > 0 have pre_slots more partials
+  // (the prefix pass's chunks) after the num_splits tail partials
+  const int* pre_pages;
+  int pre_slots;
 };
 
 template <typename T>
@@ -1269,16 +1291,17 @@ __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
   const int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
   bool has = n > 0;
   if (p.slot) has = has && load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) >= 0;
+  const int S = p.num_splits + ((p.pre_pages && p.pre_pages[b] > 0) ? p.pre_slots : 0);
   float M = -INFINITY;
   if (has) {
-    for (int s = 0; s < p.num_splits; ++s) {
+    for (int s = 0; s < S; ++s) {
       M = fmaxf(M, p.mx[b * p.ss0 + h * p.ss1 + s * p.ss2]);
     }
   }
   for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
     float L = 0.f, a = 0.f;
     if (has && M != -INFINITY) {
-      for (int s = 0; s < p.num_splits; ++s) {
+      for (int s = 0; s < S; ++s) {
         const int64_t so = b * p.ss0 + h * p.ss1 + s * p.ss2;
         const float m = p.mx[so];
         if (m == -INFINITY) continue;
@@ -1289,6 +1312,416 @@ __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
     }
     T* o = static_cast<T*>(p.out) + b * p.os0 + h * p.os1 + d * p.os2;
     *o = from_f32<T>(L > 0.f ? a / L : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// shared-prefix (cascade) pass
+// ---------------------------------------------------------------------------
+// A group is a set of sequences whose block-table rows start with the same
+// grp_pages[g] physical pages (a shared prompt prefix registered once and
+// attached to every member).  The plain decode reads those pages once per
+// member; this pass reads them once per KV head for all of the group's query
+// rows, rows = members x (q heads of the KV head).  CTA (chunk c, row block
+// rb, group g x KV head h) serves 64 rows -- one m16 tile per consumer warp,
+// every warp consuming every stage of the TMA ring -- over prefix tiles
+// [c T / C, (c + 1) T / C) of T = pages * block_size / 32, and writes its
+// rows' (max, sum, acc) into slot slot0 + c of the split workspace.  The
+// split reducer then merges these slots with the tail pass's partials
+// (same LSE merge as reference paged_decode.py:593-635).
+struct PrefixParams {
+  int num_seqs, num_kv_heads, group, block_size, num_blocks, max_blocks;
+  float scale_log2;
+  const void* q;
+  int64_t qs0, qs1, qs2;
+  int rope_dim;  // > 0: q rows are rotated by their sequence's position
+  const float* rope_inv_freq;
+  const void* rope_pos;
+  int rope_pos64;
+  int64_t rope_pos_stride;
+  const void* bt;
+  int bt64;
+  int64_t bts0, bts1;
+  const int* grp_start;    // [groups + 1], CSR into grp_members
+  const int* grp_members;  // sequence indices; the first member's table row is read
+  const int* grp_pages;    // shared pages per group (pages * block_size % 32 == 0)
+  int chunks;
+  float* pacc;
+  int64_t pas0, pas1, pas2, pas3;
+  float* pmax;
+  float* psum;
+  int64_t pss0, pss1, pss2;
+  int slot0;
+  int kperm[4], vperm[4];
+  int* status;
+  int num_stages;
+};
+
+constexpr int kPrefixRows = kConsumerWarps * 16;  // query rows per prefix CTA
+
+template <int D>
+constexpr int prefix_q_bytes() {
+  return (D / 64) * (kTile * 128);  // one warp's Q block: [D/64][32 rows][64], rows 0-15 used
+}
+
+template <int D>
+size_t prefix_smem_bytes(int stages) {
+  return 1024 + static_cast<size_t>(stages) * Smem<D>::kStageBytes +
+         kConsumerWarps * prefix_q_bytes<D>() + 2 * kPrefixRows * sizeof(int) +
+         static_cast<size_t>(stages) * 16 + 64;
+}
+
+template <typename T, int D, int kPageRows>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefix_kernel(const __grid_constant__ PrefixParams p,
+                  const __grid_constant__ CUtensorMap tmap_k,
+                  const __grid_constant__ CUtensorMap tmap_v) {
+  using SM = Smem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int NST = p.num_stages;
+  uint8_t* stages = smem;
+  uint8_t* qsm = stages + NST * SM::kStageBytes;
+  int* row_seq = reinterpret_cast<int*>(qsm + kConsumerWarps * prefix_q_bytes<D>());
+  float* row_pos = reinterpret_cast<float*>(row_seq + kPrefixRows);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(row_pos + kPrefixRows);
+  uint64_t* empty_bar = full_bar + NST;
+  int* misc = reinterpret_cast<int*>(empty_bar + NST);  // [0] abort
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  volatile int* abort_flag = misc;
+
+  if (tid < NST) {
+    mbar_init(smem_u32(&full_bar[tid]), 1);
+    mbar_init(smem_u32(&empty_bar[tid]), kConsumerWarps);  // every warp reads every stage
+    fence_mbar_init();
+  }
+  if (tid == 0) misc[0] = 0;
+  if (warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+
+  const int c = static_cast<int>(blockIdx.x);
+  const int row0 = static_cast<int>(blockIdx.y) * kPrefixRows;
+  const int g = static_cast<int>(blockIdx.z) / p.num_kv_heads;
+  const int h = static_cast<int>(blockIdx.z) - g * p.num_kv_heads;
+  const int m0 = p.grp_start[g];
+  const int rows = (p.grp_start[g + 1] - m0) * p.group;
+  const int64_t ptok = static_cast<int64_t>(p.grp_pages[g]) * p.block_size;
+  const int tiles = static_cast<int>(ptok / kTile);
+  const int t0 = static_cast<int>(static_cast<int64_t>(c) * tiles / p.chunks);
+  const int t1 = static_cast<int>(static_cast<int64_t>(c + 1) * tiles / p.chunks);
+  __syncthreads();  // barrier initialisation is visible to every warp
+  if (row0 >= rows) return;  // this group has fewer row blocks (whole CTA)
+  if (tid == 0 && c == 0 && (ptok % kTile) != 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+
+  const int bs = p.block_size;
+  const int ppt_shift = bs == 32 ? 0 : (bs == 16 ? 1 : 2);
+
+  // =========================================================================
+  // producer warp: the group's first member's pages, tile by tile
+  // =========================================================================
+  if (warp == kConsumerWarps) {
+    const int rep = p.grp_members[m0];
+    const uint64_t policy = l2_policy_evict_first();
+    const int PPT = 1 << ppt_shift;  // pages per tile
+    const int TG = max(1, min(32 >> ppt_shift, NST / 2));
+    constexpr int kOps = 2 * SM::kHalves;
+    int pst = 0;
+    uint32_t pph = 0;
+    bool bad = false;
+    for (int tg = t0; tg < t1;) {
+      const int ntile = min(TG, t1 - tg);
+      const int npage = ntile << ppt_shift;
+      const int64_t lb = (static_cast<int64_t>(tg) << ppt_shift) + lane;
+      int blk = -1;
+      if (lane < npage && lb < p.max_blocks) {
+        blk = static_cast<int>(
+            load_index(p.bt, p.bt64, static_cast<int64_t>(rep) * p.bts0 + lb * p.bts1));
+      }
+      const bool pvalid = lane < npage && blk >= 0 && blk < p.num_blocks;
+      bad = bad || (lane < npage && !pvalid);
+      const uint32_t pages = __ballot_sync(0xffffffffu, pvalid);
+      bool ok = true;
+      if (lane < ntile) {
+        int st = pst + lane;
+        uint32_t ph = pph;
+        if (st >= NST) {
+          st -= NST;
+          ph ^= 1u;
+        }
+        ok = mbar_wait(smem_u32(&empty_bar[st]), ph ^ 1u, p.status, abort_flag);
+        const uint32_t tmask = (pages >> (lane << ppt_shift)) & ((1u << PPT) - 1u);
+        if (ok) {
+          mbar_arrive_expect_tx(smem_u32(&full_bar[st]),
+                                static_cast<uint32_t>(__popc(tmask)) * (bs * D * 2 * 2));
+        }
+      }
+      if (__all_sync(0xffffffffu, ok)) {
+        if constexpr (kPageRows > 0) {
+          const int nops = npage * 2;  // one box per (page, plane)
+          for (int base = 0; base < nops; base += 32) {
+            const int op = base + lane;
+            const int page = op >> 1;
+            const int pblk = __shfl_sync(0xffffffffu, blk, page & 31);
+            if (op < nops && ((pages >> page) & 1u)) {
+              const int plane = op & 1;
+              int st = pst + (page >> ppt_shift);
+              if (st >= NST) st -= NST;
+              const uint32_t dst = smem_u32(stages + st * SM::kStageBytes) +
+                                   plane * (SM::kHalves * SM::kHalfBytes) +
+                                   (page & (PPT - 1)) * (kPageRows * 256);
+              const int* perm = plane ? p.vperm : p.kperm;
+              tma_load_5d(dst, plane ? &tmap_v : &tmap_k, smem_u32(&full_bar[st]), 0,
+                          tmap_coord(perm[0], h, pblk), tmap_coord(perm[1], h, pblk),
+                          tmap_coord(perm[2], h, pblk), tmap_coord(perm[3], h, pblk), policy);
+            }
+          }
+        } else {
+          const int nops = npage * kOps;
+          for (int base = 0; base < nops; base += 32) {
+            const int op = base + lane;
+            const int page = op / kOps;
+            const int pblk = __shfl_sync(0xffffffffu, blk, page & 31);
+            if (op < nops && ((pages >> page) & 1u)) {
+              const int rem = op - page * kOps;
+              const int plane = rem / SM::kHalves;
+              const int hh = rem - plane * SM::kHalves;
+              int st = pst + (page >> ppt_shift);
+              if (st >= NST) st -= NST;
+              const uint32_t dst = smem_u32(stages + st * SM::kStageBytes) +
+                                   plane * (SM::kHalves * SM::kHalfBytes) + hh * SM::kHalfBytes +
+                                   (((page & (PPT - 1)) * bs) << 7);
+              const int* perm = plane ? p.vperm : p.kperm;
+              tma_load_4d(dst, plane ? &tmap_v : &tmap_k, smem_u32(&full_bar[st]), hh * 64,
+                          tmap_coord(perm[0], h, pblk), tmap_coord(perm[1], h, pblk),
+                          tmap_coord(perm[2], h, pblk), policy);
+            }
+          }
+        }
+      }
+      pst += ntile;
+      if (pst >= NST) {
+        pst -= NST;
+        pph ^= 1u;
+      }
+      tg += ntile;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+    return;
+  }
+
+  // =========================================================================
+  // consumer warps: warp w owns rows row0 + 16 w .. + 15
+  // =========================================================================
+  const int g8 = lane >> 2;
+  const int t4 = lane & 3;
+  const int mi = lane >> 3;
+  const int r8 = lane & 7;
+  uint8_t* qw = qsm + warp * prefix_q_bytes<D>();
+  const int wrow0 = row0 + 16 * warp;
+  if (lane < 16) {
+    const int gr = wrow0 + lane;
+    int seq = -1;
+    float posf = 0.f;
+    if (gr < rows) {
+      seq = p.grp_members[m0 + gr / p.group];
+      if (seq < 0 || seq >= p.num_seqs) {  // not a row of q: skipped, flagged
+        atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+        seq = -1;
+      }
+      if (seq >= 0 && p.rope_dim > 0) {
+        posf = static_cast<float>(
+            load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(seq) * p.rope_pos_stride));
+      }
+    }
+    row_seq[16 * warp + lane] = seq;
+    row_pos[16 * warp + lane] = posf;
+  }
+  __syncwarp();
+  for (int e = lane; e < 16 * (D / 8); e += 32) {
+    const int r = e / (D / 8);
+    const int ch = e - r * (D / 8);
+    const int gr = wrow0 + r;
+    const int seq = row_seq[16 * warp + r];
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (seq >= 0) {
+      const int qh = h * p.group + (gr - (gr / p.group) * p.group);
+      const T* src = static_cast<const T*>(p.q) + seq * p.qs0 + qh * p.qs1 + ch * 8 * p.qs2;
+      if (p.qs2 == 1 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        __align__(16) T el[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) el[i] = src[i * p.qs2];
+        v = *reinterpret_cast<const uint4*>(el);
+      }
+    }
+    *reinterpret_cast<uint4*>(qw + chunk_offset(r, ch)) = v;
+  }
+  __syncwarp();
+  if (p.rope_dim > 0) {
+    // RoPE of the rows in place; rows of one member share their angles
+    const int half = p.rope_dim >> 1;
+    for (int i = lane; i < half; i += 32) {
+      const float invf = p.rope_inv_freq[i];
+      int last = -1;
+      float cs = 1.f, sn = 0.f;
+      for (int r = 0; r < 16; ++r) {
+        const int seq = row_seq[16 * warp + r];
+        if (seq < 0) continue;  // rows past the group's end (or invalid members)
+        if (seq != last) {
+          sincosf(__fmul_rn(row_pos[16 * warp + r], invf), &sn, &cs);
+          last = seq;
+        }
+        T* x1p = reinterpret_cast<T*>(qw + tile_offset(r, i));
+        T* x2p = reinterpret_cast<T*>(qw + tile_offset(r, i + half));
+        float y1, y2;
+        rope_rotate_pair_cs(to_f32<T>(*x1p), to_f32<T>(*x2p), cs, sn, y1, y2);
+        *x1p = from_f32<T>(y1);
+        *x2p = from_f32<T>(y2);
+      }
+    }
+    __syncwarp();
+  }
+  uint32_t qf[D / 16][4];
+  const uint32_t qbase = smem_u32(qw);
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    ldsm_x4(qbase + chunk_offset(r8 + (mi & 1) * 8, ks * 2 + (mi >> 1)), qf[ks][0], qf[ks][1],
+            qf[ks][2], qf[ks][3]);
+  }
+
+  float m0r = -INFINITY, m1r = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float o[D / 8][4];
+#pragma unroll
+  for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  int cst = 0;
+  uint32_t cph = 0;
+  for (int t = t0; t < t1; ++t) {
+    const int stage = cst;
+    const uint32_t phase = cph;
+    if (++cst == NST) {
+      cst = 0;
+      cph ^= 1u;
+    }
+    if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, abort_flag)) continue;
+    const uint32_t kbase = smem_u32(stages + stage * SM::kStageBytes);
+    const uint32_t vbase = kbase + SM::kHalves * SM::kHalfBytes;
+    // ---- S = Q K^T (16 rows x 32 tokens; every prefix token is valid) ----
+    float sacc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        const int tok = np * 16 + (mi >> 1) * 8 + r8;
+        const int chunk = ks * 2 + (mi & 1);
+        uint32_t b0a, b1a, b0b, b1b;
+        ldsm_x4(kbase + stage_chunk_offset<kPageRows>(tok, chunk), b0a, b1a, b0b, b1b);
+        mma_16816<T>(sacc[2 * np], qf[ks], b0a, b1a);
+        mma_16816<T>(sacc[2 * np + 1], qf[ks], b0b, b1b);
+      }
+    }
+    // ---- online softmax (base 2, scale folded in) ----
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sacc[j][e] *= p.scale_log2;
+        sacc[j][2 + e] *= p.scale_log2;
+        mx0 = fmaxf(mx0, sacc[j][e]);
+        mx1 = fmaxf(mx1, sacc[j][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0r, mx0);
+    const float mn1 = fmaxf(m1r, mx1);
+    const float alpha0 = exp2f(m0r - mn0);  // 0 on the first tile (m = -inf)
+    const float alpha1 = exp2f(m1r - mn1);
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sacc[j][0] = exp2f(sacc[j][0] - mn0);
+      sacc[j][1] = exp2f(sacc[j][1] - mn0);
+      sacc[j][2] = exp2f(sacc[j][2] - mn1);
+      sacc[j][3] = exp2f(sacc[j][3] - mn1);
+      ps0 += sacc[j][0] + sacc[j][1];
+      ps1 += sacc[j][2] + sacc[j][3];
+    }
+    l0 = l0 * alpha0 + ps0;
+    l1 = l1 * alpha1 + ps1;
+    m0r = mn0;
+    m1r = mn1;
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      o[j][0] *= alpha0;
+      o[j][1] *= alpha0;
+      o[j][2] *= alpha1;
+      o[j][3] *= alpha1;
+    }
+    // ---- O += P V ----
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t a[4];
+      a[0] = pack2<T>(sacc[2 * kk][0], sacc[2 * kk][1]);
+      a[1] = pack2<T>(sacc[2 * kk][2], sacc[2 * kk][3]);
+      a[2] = pack2<T>(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+      a[3] = pack2<T>(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        const int tok = kk * 16 + (mi & 1) * 8 + r8;
+        const int chunk = dp * 2 + (mi >> 1);
+        uint32_t b0a, b1a, b0b, b1b;
+        ldsm_x4_t(vbase + stage_chunk_offset<kPageRows>(tok, chunk), b0a, b1a, b0b, b1b);
+        mma_16816<T>(o[2 * dp], a, b0a, b1a);
+        mma_16816<T>(o[2 * dp + 1], a, b0b, b1b);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty_bar[stage]));
+  }
+
+  // ---- this chunk's partial of the warp's rows ----
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const int slot = p.slot0 + c;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = g8 + 8 * hr;
+    const int gr = wrow0 + r;
+    const int seq = row_seq[16 * warp + r];
+    if (seq < 0) continue;
+    const int qh = h * p.group + (gr - (gr / p.group) * p.group);
+    float* acc = p.pacc + seq * p.pas0 + qh * p.pas1 + slot * p.pas2;
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      const int d = 8 * j + 2 * t4;
+      if (p.pas3 == 1 && (reinterpret_cast<uintptr_t>(acc + d) & 7u) == 0) {
+        *reinterpret_cast<float2*>(acc + d) = make_float2(o[j][2 * hr], o[j][2 * hr + 1]);
+      } else {
+        acc[d * p.pas3] = o[j][2 * hr];
+        acc[(d + 1) * p.pas3] = o[j][2 * hr + 1];
+      }
+    }
+    if (t4 == 0) {
+      const float M = hr ? m1r : m0r;
+      const int64_t so = seq * p.pss0 + qh * p.pss1 + slot * p.pss2;
+      p.pmax[so] = (M == -INFINITY) ? -INFINITY : M * kLn2;  // natural-log units
+      p.psum[so] = hr ? l1 : l0;
+    }
   }
 }
 
@@ -1552,7 +1985,21 @@ extern "C" int fd_paged_decode_workspace(const fd_paged_decode_args* a, size_t* 
   return FD_OK;
 }
 
+namespace fd {
+namespace {
+int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, void* cuda_stream);
+}
+}  // namespace fd
+
 extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream) {
+  return fd::paged_decode_impl(a, nullptr, cuda_stream);
+}
+
+namespace fd {
+namespace {
+// fd_paged_decode; pre_pages (cascade tail pass, split schedule only) skips
+// each sequence's leading shared pages.
+int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, void* cuda_stream) {
   int rc = validate(a);
   if (rc) return rc;
   if (a->num_seqs == 0) return FD_OK;
@@ -1561,6 +2008,7 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   const Derived dv = derive(*a);
   const Plan plan = make_plan(*a, dv, *dev);
+  if (pre_pages && plan.splits == 0) return FD_ERR_INVALID_ARGUMENT;  // split schedule only
   const int grid = plan.grid;
   // split schedule: (split, head block, sequence) -- no division in-kernel
   const dim3 gdim = plan.splits == 0 ? dim3(static_cast<unsigned>(grid))
@@ -1611,6 +2059,7 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
   p.sl = a->seq_lens;
   p.sl64 = a->seq_lens_index == FD_INDEX_I64;
   p.sls = a->seq_lens_stride;
+  p.pre_pages = pre_pages;
   p.fused_append = a->append_k != nullptr;
   if (p.fused_append) {
     p.ak = a->append_k;
@@ -1730,6 +2179,9 @@ extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream)
               : dispatch<__half, 64>(tma, p, mk, mv, gdim, smem, *dev, stream);
 }
 
+}  // namespace
+}  // namespace fd
+
 extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_stream) {
   if (!a || a->struct_size != static_cast<int32_t>(sizeof(fd_split_kv_reduce_args)))
     return FD_ERR_INVALID_ARGUMENT;
@@ -1741,6 +2193,7 @@ extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_s
     return FD_ERR_INVALID_ARGUMENT;
   if (a->num_seqs == 0) return FD_OK;
   ReduceParams p;
+  std::memset(&p, 0, sizeof(p));
   p.num_seqs = a->num_seqs;
   p.num_q_heads = a->num_q_heads;
   p.head_dim = a->head_dim;
@@ -1777,4 +2230,249 @@ extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_s
     default:
       return cuda_status(launch_pdl(split_reduce_kernel<float>, grid, dim3(threads), 0, stream, p));
   }
+}
+
+// ---------------------------------------------------------------------------
+// cascade (shared-prefix) decode
+// ---------------------------------------------------------------------------
+namespace fd {
+namespace {
+
+struct CascadePlan {
+  int chunks, splits, row_blocks;
+};
+
+int cascade_check(const fd_paged_decode_args* a, const fd_cascade_args* c) {
+  int rc = validate(a);
+  if (rc) return rc;
+  if (!c || c->struct_size != static_cast<int32_t>(sizeof(fd_cascade_args)))
+    return FD_ERR_INVALID_ARGUMENT;
+  if (c->num_groups <= 0 || !c->group_start || !c->group_members || !c->group_pages ||
+      !c->seq_prefix_pages || c->max_group_members <= 0 || c->max_prefix_tiles < 0 ||
+      c->chunks < 0 || c->tail_splits < 0 || c->chunks > 256 || c->tail_splits > 256)
+    return FD_ERR_INVALID_ARGUMENT;
+  if (static_cast<int64_t>(c->num_groups) * a->num_kv_heads > 65535) return FD_ERR_UNSUPPORTED;
+  return FD_OK;
+}
+
+CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c,
+                         const Derived& dv, const DeviceInfo& dev) {
+  CascadePlan pl;
+  const int64_t rows = static_cast<int64_t>(c.max_group_members) * dv.group;
+  pl.row_blocks = static_cast<int>((rows + kPrefixRows - 1) / kPrefixRows);
+  const int64_t units = static_cast<int64_t>(c.num_groups) * a.num_kv_heads * pl.row_blocks;
+  if (c.chunks > 0) {
+    pl.chunks = c.chunks;
+  } else {
+    // about one prefix CTA per SM, at least two tiles per chunk
+    int64_t ch = (dev.num_sms + units - 1) / units;
+    ch = std::min<int64_t>(ch, std::max(1, c.max_prefix_tiles / 2));
+    pl.chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ch, 32)));
+  }
+  if (c.tail_splits > 0) {
+    pl.splits = c.tail_splits;
+  } else {
+    const int64_t pairs = static_cast<int64_t>(a.num_seqs) * dv.nhb;
+    const int64_t s = (dev.num_sms + pairs - 1) / std::max<int64_t>(1, pairs);
+    pl.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, 8)));
+  }
+  return pl;
+}
+
+size_t cascade_scratch_bytes(const fd_paged_decode_args& a, const CascadePlan& pl) {
+  return static_cast<size_t>(a.num_seqs) * a.num_q_heads * (pl.splits + pl.chunks) *
+         (a.head_dim + 2) * sizeof(float);
+}
+
+template <typename T, int D, int kPageRows>
+int launch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
+                  dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
+  auto kern = prefix_kernel<T, D, kPageRows>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  const int slot = dev.device & 63;
+  std::call_once(once[slot], [&] {
+    attr_err[slot] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          dev.max_smem_optin);
+  });
+  if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
+  return cuda_status(launch_pdl(kern, grid, dim3(kThreads), smem, stream, prm, mk, mv));
+}
+
+template <typename T, int D>
+int dispatch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
+                    dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
+  if constexpr (D == 128) {
+    if (prm.kperm[3] >= 0) {
+      return prm.block_size == 16 ? launch_prefix<T, D, 16>(prm, mk, mv, grid, smem, dev, st)
+                                  : launch_prefix<T, D, 8>(prm, mk, mv, grid, smem, dev, st);
+    }
+  }
+  return launch_prefix<T, D, 0>(prm, mk, mv, grid, smem, dev, st);
+}
+
+}  // namespace
+}  // namespace fd
+
+extern "C" int fd_cascade_workspace(const fd_paged_decode_args* a, const fd_cascade_args* c,
+                                    size_t* scratch_bytes) {
+  int rc = cascade_check(a, c);
+  if (rc) return rc;
+  const DeviceInfo* dev = current_device_info();
+  if (!dev) return FD_ERR_CUDA;
+  const CascadePlan pl = cascade_plan(*a, *c, derive(*a), *dev);
+  if (scratch_bytes) *scratch_bytes = cascade_scratch_bytes(*a, pl);
+  return FD_OK;
+}
+
+extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade_args* c,
+                                 void* cuda_stream) {
+  int rc = cascade_check(a, c);
+  if (rc) return rc;
+  if (a->num_seqs == 0) return FD_OK;
+  const DeviceInfo* dev = current_device_info();
+  if (!dev) return FD_ERR_CUDA;
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  const Derived dv = derive(*a);
+  const CascadePlan pl = cascade_plan(*a, *c, dv, *dev);
+  if (!a->scratch || a->scratch_bytes < cascade_scratch_bytes(*a, pl)) return FD_ERR_WORKSPACE;
+  const int D = a->head_dim;
+  const int64_t slots = pl.splits + pl.chunks;
+  float* acc = a->scratch;
+  float* mx = acc + static_cast<int64_t>(a->num_seqs) * a->num_q_heads * slots * D;
+  float* sm = mx + static_cast<int64_t>(a->num_seqs) * a->num_q_heads * slots;
+
+  // ---- prefix pass ----
+  PrefixParams pp;
+  std::memset(&pp, 0, sizeof(pp));
+  pp.num_seqs = a->num_seqs;
+  pp.num_kv_heads = a->num_kv_heads;
+  pp.group = dv.group;
+  pp.block_size = a->block_size;
+  pp.num_blocks = a->num_blocks;
+  pp.max_blocks = a->max_blocks_per_seq;
+  pp.scale_log2 = a->sm_scale * kLog2e;
+  pp.q = a->q;
+  pp.qs0 = a->q_stride[0];
+  pp.qs1 = a->q_stride[1];
+  pp.qs2 = a->q_stride[2];
+  if (a->rope_dim > 0) {
+    pp.rope_dim = a->rope_dim;
+    pp.rope_inv_freq = a->rope_inv_freq;
+    pp.rope_pos = a->rope_positions;
+    pp.rope_pos64 = a->rope_positions_index == FD_INDEX_I64;
+    pp.rope_pos_stride = a->rope_positions_stride;
+  }
+  pp.bt = a->block_tables;
+  pp.bt64 = a->block_tables_index == FD_INDEX_I64;
+  pp.bts0 = a->block_tables_stride[0];
+  pp.bts1 = a->block_tables_stride[1];
+  pp.grp_start = c->group_start;
+  pp.grp_members = c->group_members;
+  pp.grp_pages = c->group_pages;
+  pp.chunks = pl.chunks;
+  pp.pacc = acc;
+  pp.pas3 = 1;
+  pp.pas2 = D;
+  pp.pas1 = slots * D;
+  pp.pas0 = static_cast<int64_t>(a->num_q_heads) * slots * D;
+  pp.pmax = mx;
+  pp.psum = sm;
+  pp.pss2 = 1;
+  pp.pss1 = slots;
+  pp.pss0 = static_cast<int64_t>(a->num_q_heads) * slots;
+  pp.slot0 = pl.splits;
+  pp.status = device_status_ptr();
+  if (!pp.status) return FD_ERR_CUDA;
+  CUtensorMap mk, mv;
+  std::memset(&mk, 0, sizeof(mk));
+  std::memset(&mv, 0, sizeof(mv));
+  for (int plane = 0; plane < 2; ++plane) {
+    CacheDesc cd;
+    cd.base = plane ? a->v_cache : a->k_cache;
+    cd.elem_bytes = 2;
+    cd.is_bf16 = a->dtype == FD_DTYPE_BF16;
+    cd.head_dim = D;
+    cd.block_size = a->block_size;
+    cd.num_heads = a->num_kv_heads;
+    cd.num_blocks = a->num_blocks;
+    const int64_t* st = plane ? a->v_stride : a->k_stride;
+    for (int i = 0; i < 4; ++i) cd.stride[i] = st[i];
+    if (cd.num_heads == 1) cd.stride[1] = cd.stride[0];
+    if (!get_cache_tensor_map(cd, plane ? &mv : &mk, plane ? pp.vperm : pp.kperm))
+      return FD_ERR_UNSUPPORTED;
+  }
+  const size_t fixed = D == 128 ? prefix_smem_bytes<128>(0) : prefix_smem_bytes<64>(0);
+  const size_t stage_bytes = (D == 128 ? Smem<128>::kStageBytes : Smem<64>::kStageBytes) + 16;
+  const size_t cap = static_cast<size_t>(dev->max_smem_optin);
+  if (fixed + 2 * stage_bytes > cap) return FD_ERR_UNSUPPORTED;
+  const int stages = std::min(static_cast<int>((cap - fixed) / stage_bytes), kMaxStages);
+  pp.num_stages = stages;
+  const size_t psmem = D == 128 ? prefix_smem_bytes<128>(stages) : prefix_smem_bytes<64>(stages);
+  const dim3 pgrid(static_cast<unsigned>(pl.chunks), static_cast<unsigned>(pl.row_blocks),
+                   static_cast<unsigned>(c->num_groups * a->num_kv_heads));
+  const bool bf16 = a->dtype == FD_DTYPE_BF16;
+  if (D == 128) {
+    rc = bf16 ? dispatch_prefix<__nv_bfloat16, 128>(pp, mk, mv, pgrid, psmem, *dev, stream)
+              : dispatch_prefix<__half, 128>(pp, mk, mv, pgrid, psmem, *dev, stream);
+  } else {
+    rc = bf16 ? dispatch_prefix<__nv_bfloat16, 64>(pp, mk, mv, pgrid, psmem, *dev, stream)
+              : dispatch_prefix<__half, 64>(pp, mk, mv, pgrid, psmem, *dev, stream);
+  }
+  if (rc) return rc;
+
+  // ---- tail pass: split decode of every sequence after its shared pages ----
+  fd_paged_decode_args t = *a;
+  t.num_splits = pl.splits;
+  t.epilogue = FD_EPILOGUE_PARTIALS;
+  t.part_acc = acc;
+  t.part_acc_stride[0] = pp.pas0;
+  t.part_acc_stride[1] = pp.pas1;
+  t.part_acc_stride[2] = pp.pas2;
+  t.part_acc_stride[3] = 1;
+  t.part_max = mx;
+  t.part_sum = sm;
+  t.part_stat_stride[0] = pp.pss0;
+  t.part_stat_stride[1] = pp.pss1;
+  t.part_stat_stride[2] = 1;
+  rc = paged_decode_impl(&t, c->seq_prefix_pages, cuda_stream);
+  if (rc) return rc;
+
+  // ---- merge: tail splits + the group's prefix chunks ----
+  ReduceParams rp;
+  std::memset(&rp, 0, sizeof(rp));
+  rp.num_seqs = a->num_seqs;
+  rp.num_q_heads = a->num_q_heads;
+  rp.head_dim = D;
+  rp.num_splits = pl.splits;
+  rp.acc = acc;
+  rp.as0 = pp.pas0;
+  rp.as1 = pp.pas1;
+  rp.as2 = pp.pas2;
+  rp.as3 = 1;
+  rp.mx = mx;
+  rp.sm = sm;
+  rp.ss0 = pp.pss0;
+  rp.ss1 = pp.pss1;
+  rp.ss2 = 1;
+  rp.sl = a->seq_lens;
+  rp.sl64 = a->seq_lens_index == FD_INDEX_I64;
+  rp.sls = a->seq_lens_stride;
+  if (a->append_k) {  // rows without a cache slot get zeros (reference MASK_INVALID_SLOT)
+    rp.slot = a->slot_mapping;
+    rp.slot64 = a->slot_mapping_index == FD_INDEX_I64;
+    rp.slots = a->slot_mapping_stride;
+  }
+  rp.out = a->out;
+  rp.os0 = a->out_stride[0];
+  rp.os1 = a->out_stride[1];
+  rp.os2 = a->out_stride[2];
+  rp.pre_pages = c->seq_prefix_pages;
+  rp.pre_slots = pl.chunks;
+  const dim3 rgrid(a->num_seqs, a->num_q_heads);
+  const int threads = D >= 128 ? 128 : 64;
+  return bf16 ? cuda_status(launch_pdl(split_reduce_kernel<__nv_bfloat16>, rgrid, dim3(threads), 0,
+                                       stream, rp))
+              : cuda_status(launch_pdl(split_reduce_kernel<__half>, rgrid, dim3(threads), 0,
+                                       stream, rp));
 }

@@ -153,6 +153,37 @@ int fd_paged_decode_workspace(const fd_paged_decode_args* args, size_t* scratch_
 
 int fd_paged_decode(const fd_paged_decode_args* args, void* cuda_stream);
 
+/* ---- cascade (shared-prefix) decode -----------------------------------------
+ * Same result as fd_paged_decode(args) for a batch in which groups of
+ * sequences share the first pages of their block-table rows (a prompt prefix
+ * registered once and attached to every member: flashdec/cache.py:192-276).
+ * The shared pages are read once per KV head for all of a group's query rows
+ * (prefix pass, 64 rows per CTA), the rest of every sequence by the split
+ * decode (tail pass), and the split reducer merges both (LSE merge of
+ * flashdec/kernels/paged_decode.py:593-635): three launches on the stream.
+ * args->num_splits, epilogue and part_* are ignored; args->scratch must hold
+ * fd_cascade_workspace bytes.  Every member's seq_len must exceed its
+ * group's prefix tokens (the current token is private).  Requires caches that
+ * the TMA loader can address (token- or dim-major pages); FD_ERR_UNSUPPORTED
+ * otherwise (call fd_paged_decode instead). */
+typedef struct fd_cascade_args {
+  int32_t struct_size;             /* = sizeof(fd_cascade_args) */
+  int32_t num_groups;              /* >= 1 */
+  const int32_t* group_start;      /* [num_groups + 1] CSR offsets into group_members */
+  const int32_t* group_members;    /* sequence indices (rows of q), grouped */
+  const int32_t* group_pages;      /* [num_groups] shared pages; pages * block_size % 32 == 0 */
+  const int32_t* seq_prefix_pages; /* [num_seqs] the sequence's group_pages, 0 outside groups */
+  int32_t max_group_members;       /* host-side bound: largest group */
+  int32_t max_prefix_tiles;        /* host-side bound: largest group_pages * block_size / 32 */
+  int32_t chunks;                  /* prefix chunks per (group, kv head, 64 rows); 0: auto */
+  int32_t tail_splits;             /* splits of every sequence's tail; 0: auto */
+} fd_cascade_args;
+
+int fd_cascade_workspace(const fd_paged_decode_args* args, const fd_cascade_args* cascade,
+                         size_t* scratch_bytes);
+int fd_cascade_decode(const fd_paged_decode_args* args, const fd_cascade_args* cascade,
+                      void* cuda_stream);
+
 /* fd_paged_decode with its ticket and scratch buffers taken from 8 MiB of
  * fp32 scratch and 4096 int32 tickets that are static device storage of the
  * library (the tickets/scratch fields of `args` are ignored), for callers

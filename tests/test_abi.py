@@ -22,6 +22,7 @@ _STRUCTS = {
     "fd_paged_decode_args": _lib.PagedDecodeArgs,
     "fd_split_kv_reduce_args": _lib.SplitReduceArgs,
     "fd_rope_kv_append_args": _lib.RopeKVAppendArgs,
+    "fd_cascade_args": _lib.CascadeArgs,
 }
 
 
@@ -120,6 +121,17 @@ def test_host_argument_checks_answer_without_a_gpu(lib):
     s.struct_size = 4
     assert lib.fd_split_kv_reduce(ctypes.byref(s), None) == _lib.FD_ERR_INVALID_ARGUMENT
     assert lib.fd_selftest_wait_timeout(0, None) == _lib.FD_ERR_INVALID_ARGUMENT
+    c = _lib.CascadeArgs()
+    c.struct_size = ctypes.sizeof(c)
+    a = _lib.PagedDecodeArgs()
+    a.struct_size = ctypes.sizeof(a)
+    a.dtype, a.head_dim, a.block_size = _lib.FD_DTYPE_BF16, 128, 32
+    a.num_seqs, a.num_q_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq = 1, 8, 1, 1, 1
+    a.q = a.out = a.k_cache = a.v_cache = a.block_tables = a.seq_lens = 1
+    # no groups described
+    assert lib.fd_cascade_decode(ctypes.byref(a), ctypes.byref(c), None) == \
+        _lib.FD_ERR_INVALID_ARGUMENT
+    assert lib.fd_cascade_decode(ctypes.byref(a), None, None) == _lib.FD_ERR_INVALID_ARGUMENT
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
