@@ -62,8 +62,7 @@ class CascadeArgs(ctypes.Structure):
     _fields_ = [
         ("struct_size", _i32), ("num_groups", _i32), ("group_start", _vp),
         ("group_members", _vp), ("group_pages", _vp), ("seq_prefix_pages", _vp),
-        ("max_group_members", _i32), ("max_prefix_tiles", _i32), ("chunks", _i32),
-        ("tail_splits", _i32),
+        ("chunks", _i32), ("tail_splits", _i32),
     ]
 
 
@@ -135,7 +134,8 @@ def load_library():
         lib.fd_split_kv_reduce.argtypes = [ctypes.POINTER(SplitReduceArgs), _vp]
         lib.fd_cascade_workspace.argtypes = [ctypes.POINTER(PagedDecodeArgs),
                                              ctypes.POINTER(CascadeArgs),
-                                             ctypes.POINTER(ctypes.c_size_t)]
+                                             ctypes.POINTER(ctypes.c_size_t),
+                                             ctypes.POINTER(ctypes.c_int64)]
         lib.fd_cascade_decode.argtypes = [ctypes.POINTER(PagedDecodeArgs),
                                           ctypes.POINTER(CascadeArgs), _vp]
         lib.fd_rope_kv_append.argtypes = [ctypes.POINTER(RopeKVAppendArgs), _vp]

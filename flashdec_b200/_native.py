@@ -225,11 +225,15 @@ def paged_decode(q, k4, v4, block_tables, seq_lens, out, **kw):
 
 
 class CascadeGroups:
-    """Device description of the shared-prefix groups of a batch for
-    ``fd_cascade_decode``: ``groups`` lists the sequence indices (rows of q)
-    of each group and ``pages`` its shared leading pages (the same physical
-    pages at the start of every member's block-table row; ``pages *
-    block_size`` a multiple of 32)."""
+    """Shared-prefix groups of a batch for ``fd_cascade_decode``: ``groups``
+    lists the sequence indices (rows of q) of each group and ``pages`` its
+    shared leading pages (the same physical pages at the start of every
+    member's block-table row; ``pages * block_size`` a multiple of 32).  The
+    group description stays in host memory (the C-ABI copies it into the
+    launch); the per-sequence prefix pages go to the device once."""
+
+    MAX_GROUPS = 32
+    MAX_MEMBERS = 512
 
     def __init__(self, groups, pages, num_seqs, block_size, device):
         if len(groups) != len(pages) or not groups:
@@ -238,45 +242,50 @@ class CascadeGroups:
         members = []
         seq_pages = [0] * int(num_seqs)
         for g, pg in zip(groups, pages):
-            if (int(pg) * int(block_size)) % 32:
-                raise ValueError("shared prefix tokens must be a multiple of 32")
+            if int(pg) <= 0 or (int(pg) * int(block_size)) % 32:
+                raise ValueError("shared prefix tokens must be a positive multiple of 32")
+            if not g:
+                raise ValueError("a group needs at least one member")
             for b in g:
                 if not 0 <= int(b) < num_seqs or seq_pages[int(b)]:
                     raise ValueError("group members must be distinct rows of the batch")
                 seq_pages[int(b)] = int(pg)
             members += [int(b) for b in g]
             start.append(len(members))
-        host = torch.tensor(start + members + [int(x) for x in pages] + seq_pages,
-                            dtype=torch.int32)
-        self.data = host.pin_memory().to(device, non_blocking=True) \
-            if torch.device(device).type == "cuda" else host
-        ng, nm = len(groups), len(members)
-        self.args = _lib.CascadeArgs()
-        a = self.args
+        if len(groups) > self.MAX_GROUPS or len(members) > self.MAX_MEMBERS:
+            raise ValueError(f"at most {self.MAX_GROUPS} groups and {self.MAX_MEMBERS} members")
+        self.host_start = (ctypes.c_int32 * len(start))(*start)
+        self.host_members = (ctypes.c_int32 * len(members))(*members)
+        self.host_pages = (ctypes.c_int32 * len(pages))(*[int(x) for x in pages])
+        seq = torch.tensor(seq_pages, dtype=torch.int32)
+        self.seq_pages = seq.pin_memory().to(device, non_blocking=True) \
+            if torch.device(device).type == "cuda" else seq
+        a = self.args = _lib.CascadeArgs()
         a.struct_size = ctypes.sizeof(_lib.CascadeArgs)
-        a.num_groups = ng
-        base, esz = self.data.data_ptr(), 4
-        a.group_start = base
-        a.group_members = base + (ng + 1) * esz
-        a.group_pages = base + (ng + 1 + nm) * esz
-        a.seq_prefix_pages = base + (ng + 1 + nm + ng) * esz
-        a.max_group_members = max(len(g) for g in groups)
-        a.max_prefix_tiles = max(int(pg) * int(block_size) // 32 for pg in pages)
+        a.num_groups = len(groups)
+        a.group_start = ctypes.addressof(self.host_start)
+        a.group_members = ctypes.addressof(self.host_members)
+        a.group_pages = ctypes.addressof(self.host_pages)
+        a.seq_prefix_pages = self.seq_pages.data_ptr()
 
 
-def cascade_workspace_bytes(decode_args, cascade_args):
+def cascade_workspace(decode_args, cascade_args):
+    """(scratch bytes, ticket entries) ``fd_cascade_decode`` needs."""
     lib = _lib.load_library()
     nbytes = ctypes.c_size_t(0)
+    tickets = ctypes.c_int64(0)
     _lib.check(lib.fd_cascade_workspace(ctypes.byref(decode_args), ctypes.byref(cascade_args),
-                                        ctypes.byref(nbytes)), "fd_cascade_workspace")
-    return nbytes.value
+                                        ctypes.byref(nbytes), ctypes.byref(tickets)),
+               "fd_cascade_workspace")
+    return nbytes.value, tickets.value
 
 
 def cascade_decode(q, k4, v4, block_tables, seq_lens, out, groups, *, sm_scale, block_size,
                    num_seqs, chunks=0, tail_splits=0, append_k=None, append_v=None,
                    slot_mapping=None, rope=None):
-    """Launch ``fd_cascade_decode`` (prefix pass, tail pass, merge) on the
-    current stream; ``groups`` is a :class:`CascadeGroups`.  Returns ``out``."""
+    """Launch ``fd_cascade_decode`` (prefix pass, then the tail pass with the
+    merge) on the current stream; ``groups`` is a :class:`CascadeGroups`.
+    Returns ``out``."""
     prep = prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, sm_scale=sm_scale,
                                 block_size=block_size, num_seqs=num_seqs, num_splits=1,
                                 append_k=append_k, append_v=append_v,
@@ -284,9 +293,10 @@ def cascade_decode(q, k4, v4, block_tables, seq_lens, out, groups, *, sm_scale, 
     a = prep.args
     c = groups.args
     c.chunks, c.tail_splits = int(chunks), int(tail_splits)
-    nbytes = cascade_workspace_bytes(a, c)
-    _, scratch = workspace(q.device, 0, nbytes)
+    nbytes, ntickets = cascade_workspace(a, c)
+    tickets, scratch = workspace(q.device, ntickets, nbytes)
     a.scratch, a.scratch_bytes = scratch.data_ptr(), scratch.numel() * 4
+    a.tickets, a.tickets_capacity = tickets.data_ptr(), tickets.numel()
     _lib.check(prep.lib.fd_cascade_decode(ctypes.byref(a), ctypes.byref(c),
                                           ctypes.c_void_p(stream_handle(q.device))),
                "fd_cascade_decode")

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from dataclasses import dataclass, replace
 from typing import Hashable
 
@@ -55,8 +56,9 @@ class _DeviceMeta:
     :class:`_BlockTableCache` and is shared with earlier transactions while
     its rows are unchanged."""
 
-    def __init__(self, device, positions, locations, table, block_size):
+    def __init__(self, device, positions, locations, table, block_size, cascade=None):
         n = len(positions)
+        self.cascade = cascade  # _native.CascadeGroups of the batch's shared prefixes, or None
         packed = np.empty(4 * n * 8 + n * 4, np.uint8)
         i64 = packed[:4 * n * 8].view(np.int64)
         i64[:n] = positions
@@ -128,11 +130,61 @@ class _BlockTableCache:
         return table
 
 
+def _cascade_enabled():
+    # Opt-in: on the Qwen c5 shape (16 rows sharing 4096 tokens) the prefix
+    # pass + tail pass measure 28-34 us per layer against 24 us for the plain
+    # decode, whose shared-page re-reads hit L2; the prefix pass is bound by
+    # mma.sync latency, not by memory.
+    return os.environ.get("FLASHDEC_B200_CASCADE", "0") == "1"
+
+
+class _CascadeCache:
+    """Shared-prefix groups of the last transaction's rows (device copy).
+
+    Rows of one transaction whose requests are attached to the same
+    registered prefix start their block tables with the same physical pages
+    (``shared_block_count`` of them).  With FLASHDEC_B200_CASCADE=1, groups
+    of at least two rows with at least 128 shared tokens go to
+    ``fd_cascade_decode``; the shared length is
+    rounded down to whole 32-token tiles (the rest is read as private
+    tokens).  The description only changes when the rows or their prefixes
+    do, so it is rebuilt only then."""
+
+    MIN_MEMBERS = 2
+    MIN_TOKENS = 128
+
+    def __init__(self):
+        self.key = None
+        self.groups = None
+
+    def get(self, device, ids, requests, block_size):
+        attached = tuple((requests[r].prefix_id, requests[r].shared_block_count) for r in ids)
+        key = (ids, attached)
+        if key == self.key:
+            return self.groups
+        unit = 32 // math.gcd(32, block_size)  # pages per 32-token tile
+        by_prefix = {}
+        for row, (pid, count) in enumerate(attached):
+            if pid is not None and count > 0:
+                by_prefix.setdefault(pid, (count, []))[1].append(row)
+        rows, pages = [], []
+        for count, members in by_prefix.values():
+            shared = (count // unit) * unit
+            if len(members) >= self.MIN_MEMBERS and shared * block_size >= self.MIN_TOKENS:
+                rows.append(members)
+                pages.append(shared)
+        self.groups = (_native.CascadeGroups(rows, pages, len(ids), block_size, device)
+                       if rows else None)
+        self.key = key
+        return self.groups
+
+
 class _FusedLayerLauncher:
     """Launch state of the engine's fused layer step for one open token.
 
-    A layer is ONE ``fd_paged_decode`` launch with the fused append and RoPE
-    fields set: the kernel rotates q and the new K row by the transaction's
+    A layer is ONE ``fd_paged_decode`` launch (``fd_cascade_decode`` when rows
+    share a registered prefix: see :class:`_CascadeCache`) with the fused
+    append and RoPE fields set: the kernel rotates q and the new K row by the transaction's
     positions, stores the rotated K and the raw V row at the reserved slot
     (``block_id * block_size + offset``) and attends over the sequence with
     that row -- the same arithmetic as ``fd_rope_kv_append`` followed by
@@ -197,9 +249,14 @@ class _FusedLayerLauncher:
         da.q = da.out = da.k_cache = da.v_cache = da.append_k = da.append_v = 1
         scratch = ctypes.c_size_t(0)
         tickets = ctypes.c_int64(0)
-        self.check(self.lib.fd_paged_decode_workspace(ctypes.byref(da), ctypes.byref(scratch),
-                                                      ctypes.byref(tickets)),
-                   "fd_paged_decode_workspace")
+        self.cascade = meta.cascade
+        if self.cascade is not None:
+            # shared prefixes: prefix pass, then the tail pass with the merge
+            scratch.value, tickets.value = _native.cascade_workspace(da, self.cascade.args)
+        else:
+            self.check(self.lib.fd_paged_decode_workspace(ctypes.byref(da), ctypes.byref(scratch),
+                                                          ctypes.byref(tickets)),
+                       "fd_paged_decode_workspace")
         self.workspace = (None, None)
         if scratch.value or tickets.value:
             # held here so that a later growth of the shared per-device
@@ -235,9 +292,13 @@ class _FusedLayerLauncher:
                                                   v.data_ptr())
         da.k_cache = self.k_base + layer_idx * self.k_layer_bytes
         da.v_cache = self.v_base + layer_idx * self.v_layer_bytes
-        self.check(self.lib.fd_paged_decode(ctypes.byref(da),
-                                            ctypes.c_void_p(_native.stream_handle(self.device))),
-                   "fd_paged_decode")
+        stream = ctypes.c_void_p(_native.stream_handle(self.device))
+        if self.cascade is not None:
+            self.check(self.lib.fd_cascade_decode(ctypes.byref(da),
+                                                  ctypes.byref(self.cascade.args), stream),
+                       "fd_cascade_decode")
+        else:
+            self.check(self.lib.fd_paged_decode(ctypes.byref(da), stream), "fd_paged_decode")
         return out
 
 
@@ -277,6 +338,7 @@ class PagedKVCache:
         self.v_cache = torch.zeros_like(self.k_cache)
         self.device = self.k_cache.device
         self._tables = _BlockTableCache()
+        self._cascades = _CascadeCache()
 
     # ----------------------------------------------------------- lifecycle
     def add_request(self, request_id):
@@ -405,8 +467,11 @@ class PagedKVCache:
         try:
             table = self._tables.get(self.device, ids,
                                      [self._ledger.requests[r].block_ids for r in ids])
+            cascade = (self._cascades.get(self.device, ids, self._ledger.requests,
+                                          self.block_size)
+                       if self.device.type == "cuda" and _cascade_enabled() else None)
             tx.device_view = _DeviceMeta(self.device, tx.positions, tx.locations, table,
-                                         self.block_size)
+                                         self.block_size, cascade)
         except Exception:
             self._ledger.abort_token(tx)
             raise

@@ -107,8 +107,11 @@ struct AttnParams {
   int rope_pos64;
   int64_t rope_pos_stride;
   // cascade tail pass: sequence b attends only to its tokens after its first
-  // pre_pages[b] pages (a shared prefix handled by the prefix pass)
+  // pre_pages[b] pages (a shared prefix handled by the prefix pass), and the
+  // final merge of a member (pre_pages[b] > 0) also takes the prefix pass's
+  // pre_slots partials in split slots [num_splits, num_splits + pre_slots)
   const int* pre_pages;
+  int pre_slots;
   int num_splits;  // 0 = length-balanced (stream-K) schedule
   int epilogue;    // FD_EPILOGUE_*
   int balanced;    // split mode: equal tile ranges instead of cdiv chunks
@@ -197,14 +200,18 @@ __device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
   int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
   const int64_t cap = static_cast<int64_t>(p.max_blocks) * p.block_size;
   n = n < 0 ? 0 : (n > cap ? cap : n);
+  bool live = true;
   if constexpr (kAppend) {
     // the slot is read alongside the length (one memory round trip)
     const int64_t slot = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
-    if (slot < 0) n = 0;
+    if (slot < 0) {
+      n = 0;
+      live = false;  // reference MASK_INVALID_SLOT: a zero row, no prefix either
+    }
   }
   SeqInfo r;
   r.off = 0;
-  if (p.pre_pages) {
+  if (p.pre_pages && live) {
     // cascade tail: the first pre_pages[b] pages are attended by the prefix pass
     const int off = min(max(p.pre_pages[b], 0), p.max_blocks);
     const int64_t skip = static_cast<int64_t>(off) * p.block_size;
@@ -220,6 +227,7 @@ __device__ __forceinline__ SeqInfo seq_info(const AttnParams& p, int b) {
 struct Segment {
   int b, hb, t0, t1, n, tiles;
   int off;        // block-table pages before tile 0 (cascade tail pass)
+  int extra;      // cascade member: prefix-pass partials merged after the nseg splits
   int whole;      // covers the whole pair: write the output directly
   int part_slot;  // stream-K slot id or split index
   int nseg;       // contributors to the pair's ticket
@@ -317,6 +325,7 @@ __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Seg
     s.part_slot = static_cast<int>(blockIdx.x) + b * p.nhb + hb;
     s.n = sc.seqn[b];
     s.off = 0;  // (the cascade tail pass runs the split schedule)
+    s.extra = 0;
     sc.x = seg_end;
     return true;
   }
@@ -330,9 +339,10 @@ __device__ __forceinline__ bool next_segment(const AttnParams& p, Sched& sc, Seg
   const SeqInfo si = seq_info<kAppend>(p, s.b);
   s.n = si.n;
   s.off = si.off;
+  s.extra = si.off > 0 ? p.pre_slots : 0;
   s.tiles = si.tiles;
   split_range(p, split, si.tiles, s.t0, s.t1);
-  s.whole = (S == 1) && p.epilogue == FD_EPILOGUE_FUSED;
+  s.whole = (S == 1) && p.epilogue == FD_EPILOGUE_FUSED && s.extra == 0;
   s.part_slot = split;
   s.nseg = S;
   s.c_first = 0;
@@ -1172,7 +1182,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             L[q] = 0.f;
             A[q][0] = A[q][1] = A[q][2] = A[q][3] = 0.f;
           }
-          for (int i0 = 0; i0 < s.nseg; i0 += kMergeBatch) {
+          const int nmerge = s.nseg + s.extra;  // + the prefix pass's chunks
+          for (int i0 = 0; i0 < nmerge; i0 += kMergeBatch) {
             float mv[kRowPass][kMergeBatch], lv[kRowPass][kMergeBatch];
             float4 av[kRowPass][kMergeBatch];
 #pragma unroll
@@ -1184,7 +1195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 lv[q][j] = 0.f;
                 av[q][j] = make_float4(0.f, 0.f, 0.f, 0.f);
                 const int i = i0 + j;
-                if (r < nrows && i < s.nseg) {
+                if (r < nrows && i < nmerge) {
                   const int sl = (p.num_splits == 0) ? (s.c_first + i + pid) : i;
                   const PartRef<D> pr = part_ref<D>(p, s, sl, r, head0 + r);
                   mv[q][j] = __ldcg(pr.m);
@@ -1276,39 +1287,79 @@ struct ReduceParams {
   int64_t slots;
   void* out;
   int64_t os0, os1, os2;
-  // cascade: sequences with pre_pages[b] > 0 have pre_slots more partials
-  // (the prefix pass's chunks) after the num_splits tail partials
-  const int* pre_pages;
-  int pre_slots;
 };
 
+constexpr int kReduceMaxSlots = 512;
+
+__device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
+  // blockDim.x <= 128 (at most 4 warps)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float y = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, y) : v + y;
+  }
+  const int warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  __syncthreads();  // red is free (an earlier reduction has been read)
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < nw; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  return r;
+}
+
+// One CTA per (sequence, q head); thread = dimension.  The slot maxima and
+// weights are formed once per row in shared memory, then every thread sums
+// its dimension over the slots with eight independent loads in flight, so a
+// row with many partials costs a few memory round trips instead of one per
+// partial.
 template <typename T>
 __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
+  __shared__ float w_sh[kReduceMaxSlots];
+  __shared__ float red[32];
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
   const int h = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int nt = blockDim.x;
   const int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
   bool has = n > 0;
   if (p.slot) has = has && load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) >= 0;
-  const int S = p.num_splits + ((p.pre_pages && p.pre_pages[b] > 0) ? p.pre_slots : 0);
-  float M = -INFINITY;
+  const int S = min(p.num_splits, kReduceMaxSlots);
+  const int64_t so = b * p.ss0 + h * p.ss1;
+  float mloc = -INFINITY;
   if (has) {
-    for (int s = 0; s < S; ++s) {
-      M = fmaxf(M, p.mx[b * p.ss0 + h * p.ss1 + s * p.ss2]);
-    }
+    for (int s = tid; s < S; s += nt) mloc = fmaxf(mloc, p.mx[so + s * p.ss2]);
   }
-  for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
-    float L = 0.f, a = 0.f;
+  const float M = block_reduce(mloc, red, true);
+  float lloc = 0.f;
+  for (int s = tid; s < S; s += nt) {
+    float w = 0.f;
     if (has && M != -INFINITY) {
-      for (int s = 0; s < S; ++s) {
-        const int64_t so = b * p.ss0 + h * p.ss1 + s * p.ss2;
-        const float m = p.mx[so];
-        if (m == -INFINITY) continue;
-        const float w = exp2f((m - M) * kLog2e);
-        L += w * p.sm[so];
-        a += w * p.acc[b * p.as0 + h * p.as1 + s * p.as2 + d * p.as3];
+      const float m = p.mx[so + s * p.ss2];
+      if (m != -INFINITY) {
+        w = exp2f((m - M) * kLog2e);
+        lloc += w * p.sm[so + s * p.ss2];
       }
+    }
+    w_sh[s] = w;
+  }
+  const float L = block_reduce(lloc, red, false);  // its barriers publish w_sh
+  const float* ab = p.acc + b * p.as0 + h * p.as1;
+  for (int d = tid; d < p.head_dim; d += nt) {
+    const float* ad = ab + d * p.as3;
+    float a = 0.f;
+    int s = 0;
+    for (; s + 8 <= S; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = w_sh[s + j] != 0.f ? ad[(s + j) * p.as2] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a += w_sh[s + j] * v[j];
+    }
+    for (; s < S; ++s) {
+      if (w_sh[s] != 0.f) a += w_sh[s] * ad[s * p.as2];
     }
     T* o = static_cast<T*>(p.out) + b * p.os0 + h * p.os1 + d * p.os2;
     *o = from_f32<T>(L > 0.f ? a / L : 0.f);
@@ -1323,12 +1374,15 @@ __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
 // attached to every member).  The plain decode reads those pages once per
 // member; this pass reads them once per KV head for all of the group's query
 // rows, rows = members x (q heads of the KV head).  CTA (chunk c, row block
-// rb, group g x KV head h) serves 64 rows -- one m16 tile per consumer warp,
+// rb, group g x KV head h) serves 128 rows -- one m16 tile per consumer warp,
 // every warp consuming every stage of the TMA ring -- over prefix tiles
 // [c T / C, (c + 1) T / C) of T = pages * block_size / 32, and writes its
 // rows' (max, sum, acc) into slot slot0 + c of the split workspace.  The
 // split reducer then merges these slots with the tail pass's partials
 // (same LSE merge as reference paged_decode.py:593-635).
+constexpr int kCascadeMaxGroups = 32;
+constexpr int kCascadeMaxMembers = 512;
+
 struct PrefixParams {
   int num_seqs, num_kv_heads, group, block_size, num_blocks, max_blocks;
   float scale_log2;
@@ -1342,9 +1396,12 @@ struct PrefixParams {
   const void* bt;
   int bt64;
   int64_t bts0, bts1;
-  const int* grp_start;    // [groups + 1], CSR into grp_members
-  const int* grp_members;  // sequence indices; the first member's table row is read
-  const int* grp_pages;    // shared pages per group (pages * block_size % 32 == 0)
+  // the groups travel in the launch parameters (no dependent loads before
+  // the first page): CSR offsets, member sequence indices (the first
+  // member's table row is read), shared pages (pages * block_size % 32 == 0)
+  int grp_start[kCascadeMaxGroups + 1];
+  int grp_pages[kCascadeMaxGroups];
+  int grp_members[kCascadeMaxMembers];
   int chunks;
   float* pacc;
   int64_t pas0, pas1, pas2, pas3;
@@ -1357,7 +1414,11 @@ struct PrefixParams {
   int num_stages;
 };
 
-constexpr int kPrefixRows = kConsumerWarps * 16;  // query rows per prefix CTA
+// Eight consumer warps (two per SM sub-partition, so one warp's mma and
+// exp2 latencies hide behind the other's) plus the producer warp.
+constexpr int kPrefixWarps = 8;
+constexpr int kPrefixThreads = 32 * kPrefixWarps + 32;
+constexpr int kPrefixRows = kPrefixWarps * 16;  // query rows per prefix CTA
 
 template <int D>
 constexpr int prefix_q_bytes() {
@@ -1367,12 +1428,12 @@ constexpr int prefix_q_bytes() {
 template <int D>
 size_t prefix_smem_bytes(int stages) {
   return 1024 + static_cast<size_t>(stages) * Smem<D>::kStageBytes +
-         kConsumerWarps * prefix_q_bytes<D>() + 2 * kPrefixRows * sizeof(int) +
+         kPrefixWarps * prefix_q_bytes<D>() + 2 * kPrefixRows * sizeof(int) +
          static_cast<size_t>(stages) * 16 + 64;
 }
 
 template <typename T, int D, int kPageRows>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPrefixThreads, 1)
     prefix_kernel(const __grid_constant__ PrefixParams p,
                   const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v) {
@@ -1383,7 +1444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NST = p.num_stages;
   uint8_t* stages = smem;
   uint8_t* qsm = stages + NST * SM::kStageBytes;
-  int* row_seq = reinterpret_cast<int*>(qsm + kConsumerWarps * prefix_q_bytes<D>());
+  int* row_seq = reinterpret_cast<int*>(qsm + kPrefixWarps * prefix_q_bytes<D>());
   float* row_pos = reinterpret_cast<float*>(row_seq + kPrefixRows);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(row_pos + kPrefixRows);
   uint64_t* empty_bar = full_bar + NST;
@@ -1395,11 +1456,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid < NST) {
     mbar_init(smem_u32(&full_bar[tid]), 1);
-    mbar_init(smem_u32(&empty_bar[tid]), kConsumerWarps);  // every warp reads every stage
+    mbar_init(smem_u32(&empty_bar[tid]), kPrefixWarps);  // every warp reads every stage
     fence_mbar_init();
   }
   if (tid == 0) misc[0] = 0;
-  if (warp == kConsumerWarps && lane == 0) {
+  if (warp == kPrefixWarps && lane == 0) {
     prefetch_tensormap(&tmap_k);
     prefetch_tensormap(&tmap_v);
   }
@@ -1418,7 +1479,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t1 = static_cast<int>(static_cast<int64_t>(c + 1) * tiles / p.chunks);
   __syncthreads();  // barrier initialisation is visible to every warp
   if (row0 >= rows) return;  // this group has fewer row blocks (whole CTA)
-  if (tid == 0 && c == 0 && (ptok % kTile) != 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
 
   const int bs = p.block_size;
   const int ppt_shift = bs == 32 ? 0 : (bs == 16 ? 1 : 2);
@@ -1426,7 +1486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // =========================================================================
   // producer warp: the group's first member's pages, tile by tile
   // =========================================================================
-  if (warp == kConsumerWarps) {
+  if (warp == kPrefixWarps) {
     const int rep = p.grp_members[m0];
     const uint64_t policy = l2_policy_evict_first();
     const int PPT = 1 << ppt_shift;  // pages per tile
@@ -1530,12 +1590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int seq = -1;
     float posf = 0.f;
     if (gr < rows) {
-      seq = p.grp_members[m0 + gr / p.group];
-      if (seq < 0 || seq >= p.num_seqs) {  // not a row of q: skipped, flagged
-        atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
-        seq = -1;
-      }
-      if (seq >= 0 && p.rope_dim > 0) {
+      seq = p.grp_members[m0 + gr / p.group];  // checked on the host
+      if (p.rope_dim > 0) {
         posf = static_cast<float>(
             load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(seq) * p.rope_pos_stride));
       }
@@ -1987,19 +2043,22 @@ extern "C" int fd_paged_decode_workspace(const fd_paged_decode_args* a, size_t* 
 
 namespace fd {
 namespace {
-int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, void* cuda_stream);
+int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int pre_slots,
+                      void* cuda_stream);
 }
 }  // namespace fd
 
 extern "C" int fd_paged_decode(const fd_paged_decode_args* a, void* cuda_stream) {
-  return fd::paged_decode_impl(a, nullptr, cuda_stream);
+  return fd::paged_decode_impl(a, nullptr, 0, cuda_stream);
 }
 
 namespace fd {
 namespace {
 // fd_paged_decode; pre_pages (cascade tail pass, split schedule only) skips
-// each sequence's leading shared pages.
-int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, void* cuda_stream) {
+// each sequence's leading shared pages, and a member's final merge also takes
+// the pre_slots prefix partials after the split partials.
+int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int pre_slots,
+                      void* cuda_stream) {
   int rc = validate(a);
   if (rc) return rc;
   if (a->num_seqs == 0) return FD_OK;
@@ -2060,6 +2119,7 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, void*
   p.sl64 = a->seq_lens_index == FD_INDEX_I64;
   p.sls = a->seq_lens_stride;
   p.pre_pages = pre_pages;
+  p.pre_slots = pre_pages ? pre_slots : 0;
   p.fused_append = a->append_k != nullptr;
   if (p.fused_append) {
     p.ak = a->append_k;
@@ -2189,6 +2249,7 @@ extern "C" int fd_split_kv_reduce(const fd_split_kv_reduce_args* a, void* cuda_s
     return FD_ERR_UNSUPPORTED;
   if (a->num_seqs < 0 || a->num_q_heads <= 0 || a->head_dim <= 0 || a->num_splits <= 0)
     return FD_ERR_INVALID_ARGUMENT;
+  if (a->num_splits > kReduceMaxSlots) return FD_ERR_UNSUPPORTED;
   if (!a->part_acc || !a->part_max || !a->part_sum || !a->seq_lens || !a->out)
     return FD_ERR_INVALID_ARGUMENT;
   if (a->num_seqs == 0) return FD_OK;
@@ -2242,15 +2303,31 @@ struct CascadePlan {
   int chunks, splits, row_blocks;
 };
 
+// Host checks of the group description (it is copied into the prefix
+// kernel's launch parameters).
 int cascade_check(const fd_paged_decode_args* a, const fd_cascade_args* c) {
   int rc = validate(a);
   if (rc) return rc;
   if (!c || c->struct_size != static_cast<int32_t>(sizeof(fd_cascade_args)))
     return FD_ERR_INVALID_ARGUMENT;
   if (c->num_groups <= 0 || !c->group_start || !c->group_members || !c->group_pages ||
-      !c->seq_prefix_pages || c->max_group_members <= 0 || c->max_prefix_tiles < 0 ||
-      c->chunks < 0 || c->tail_splits < 0 || c->chunks > 256 || c->tail_splits > 256)
+      !c->seq_prefix_pages || c->chunks < 0 || c->tail_splits < 0 || c->chunks > 256 ||
+      c->tail_splits > 256)
     return FD_ERR_INVALID_ARGUMENT;
+  if (c->num_groups > kCascadeMaxGroups) return FD_ERR_UNSUPPORTED;
+  if (c->group_start[0] != 0) return FD_ERR_INVALID_ARGUMENT;
+  const int total = c->group_start[c->num_groups];
+  if (total > kCascadeMaxMembers) return FD_ERR_UNSUPPORTED;
+  for (int g = 0; g < c->num_groups; ++g) {
+    if (c->group_start[g + 1] <= c->group_start[g]) return FD_ERR_INVALID_ARGUMENT;
+    const int64_t tok = static_cast<int64_t>(c->group_pages[g]) * a->block_size;
+    if (c->group_pages[g] <= 0 || c->group_pages[g] > a->max_blocks_per_seq || tok % kTile)
+      return FD_ERR_INVALID_ARGUMENT;
+  }
+  for (int i = 0; i < total; ++i) {
+    if (c->group_members[i] < 0 || c->group_members[i] >= a->num_seqs)
+      return FD_ERR_INVALID_ARGUMENT;
+  }
   if (static_cast<int64_t>(c->num_groups) * a->num_kv_heads > 65535) return FD_ERR_UNSUPPORTED;
   return FD_OK;
 }
@@ -2258,7 +2335,12 @@ int cascade_check(const fd_paged_decode_args* a, const fd_cascade_args* c) {
 CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c,
                          const Derived& dv, const DeviceInfo& dev) {
   CascadePlan pl;
-  const int64_t rows = static_cast<int64_t>(c.max_group_members) * dv.group;
+  int max_members = 0, max_tiles = 0;
+  for (int g = 0; g < c.num_groups; ++g) {
+    max_members = std::max(max_members, c.group_start[g + 1] - c.group_start[g]);
+    max_tiles = std::max(max_tiles, c.group_pages[g] * a.block_size / kTile);
+  }
+  const int64_t rows = static_cast<int64_t>(max_members) * dv.group;
   pl.row_blocks = static_cast<int>((rows + kPrefixRows - 1) / kPrefixRows);
   const int64_t units = static_cast<int64_t>(c.num_groups) * a.num_kv_heads * pl.row_blocks;
   if (c.chunks > 0) {
@@ -2266,7 +2348,7 @@ CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c
   } else {
     // about one prefix CTA per SM, at least two tiles per chunk
     int64_t ch = (dev.num_sms + units - 1) / units;
-    ch = std::min<int64_t>(ch, std::max(1, c.max_prefix_tiles / 2));
+    ch = std::min<int64_t>(ch, std::max(1, max_tiles / 2));
     pl.chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ch, 32)));
   }
   if (c.tail_splits > 0) {
@@ -2296,7 +2378,7 @@ int launch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensor
                                           dev.max_smem_optin);
   });
   if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
-  return cuda_status(launch_pdl(kern, grid, dim3(kThreads), smem, stream, prm, mk, mv));
+  return cuda_status(launch_pdl(kern, grid, dim3(kPrefixThreads), smem, stream, prm, mk, mv));
 }
 
 template <typename T, int D>
@@ -2315,13 +2397,15 @@ int dispatch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtens
 }  // namespace fd
 
 extern "C" int fd_cascade_workspace(const fd_paged_decode_args* a, const fd_cascade_args* c,
-                                    size_t* scratch_bytes) {
+                                    size_t* scratch_bytes, int64_t* tickets_needed) {
   int rc = cascade_check(a, c);
   if (rc) return rc;
   const DeviceInfo* dev = current_device_info();
   if (!dev) return FD_ERR_CUDA;
-  const CascadePlan pl = cascade_plan(*a, *c, derive(*a), *dev);
+  const Derived dv = derive(*a);
+  const CascadePlan pl = cascade_plan(*a, *c, dv, *dev);
   if (scratch_bytes) *scratch_bytes = cascade_scratch_bytes(*a, pl);
+  if (tickets_needed) *tickets_needed = static_cast<int64_t>(a->num_seqs) * dv.nhb;
   return FD_OK;
 }
 
@@ -2336,6 +2420,8 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   const Derived dv = derive(*a);
   const CascadePlan pl = cascade_plan(*a, *c, dv, *dev);
   if (!a->scratch || a->scratch_bytes < cascade_scratch_bytes(*a, pl)) return FD_ERR_WORKSPACE;
+  if (!a->tickets || a->tickets_capacity < static_cast<int64_t>(a->num_seqs) * dv.nhb)
+    return FD_ERR_WORKSPACE;
   const int D = a->head_dim;
   const int64_t slots = pl.splits + pl.chunks;
   float* acc = a->scratch;
@@ -2367,9 +2453,9 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   pp.bt64 = a->block_tables_index == FD_INDEX_I64;
   pp.bts0 = a->block_tables_stride[0];
   pp.bts1 = a->block_tables_stride[1];
-  pp.grp_start = c->group_start;
-  pp.grp_members = c->group_members;
-  pp.grp_pages = c->group_pages;
+  for (int g = 0; g <= c->num_groups; ++g) pp.grp_start[g] = c->group_start[g];
+  for (int g = 0; g < c->num_groups; ++g) pp.grp_pages[g] = c->group_pages[g];
+  for (int i = 0; i < c->group_start[c->num_groups]; ++i) pp.grp_members[i] = c->group_members[i];
   pp.chunks = pl.chunks;
   pp.pacc = acc;
   pp.pas3 = 1;
@@ -2421,10 +2507,11 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   }
   if (rc) return rc;
 
-  // ---- tail pass: split decode of every sequence after its shared pages ----
+  // ---- tail pass: split decode after the shared pages; the pair's last
+  // CTA merges the tail splits and (members) the prefix chunks ----
   fd_paged_decode_args t = *a;
   t.num_splits = pl.splits;
-  t.epilogue = FD_EPILOGUE_PARTIALS;
+  t.epilogue = FD_EPILOGUE_FUSED;
   t.part_acc = acc;
   t.part_acc_stride[0] = pp.pas0;
   t.part_acc_stride[1] = pp.pas1;
@@ -2435,44 +2522,5 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   t.part_stat_stride[0] = pp.pss0;
   t.part_stat_stride[1] = pp.pss1;
   t.part_stat_stride[2] = 1;
-  rc = paged_decode_impl(&t, c->seq_prefix_pages, cuda_stream);
-  if (rc) return rc;
-
-  // ---- merge: tail splits + the group's prefix chunks ----
-  ReduceParams rp;
-  std::memset(&rp, 0, sizeof(rp));
-  rp.num_seqs = a->num_seqs;
-  rp.num_q_heads = a->num_q_heads;
-  rp.head_dim = D;
-  rp.num_splits = pl.splits;
-  rp.acc = acc;
-  rp.as0 = pp.pas0;
-  rp.as1 = pp.pas1;
-  rp.as2 = pp.pas2;
-  rp.as3 = 1;
-  rp.mx = mx;
-  rp.sm = sm;
-  rp.ss0 = pp.pss0;
-  rp.ss1 = pp.pss1;
-  rp.ss2 = 1;
-  rp.sl = a->seq_lens;
-  rp.sl64 = a->seq_lens_index == FD_INDEX_I64;
-  rp.sls = a->seq_lens_stride;
-  if (a->append_k) {  // rows without a cache slot get zeros (reference MASK_INVALID_SLOT)
-    rp.slot = a->slot_mapping;
-    rp.slot64 = a->slot_mapping_index == FD_INDEX_I64;
-    rp.slots = a->slot_mapping_stride;
-  }
-  rp.out = a->out;
-  rp.os0 = a->out_stride[0];
-  rp.os1 = a->out_stride[1];
-  rp.os2 = a->out_stride[2];
-  rp.pre_pages = c->seq_prefix_pages;
-  rp.pre_slots = pl.chunks;
-  const dim3 rgrid(a->num_seqs, a->num_q_heads);
-  const int threads = D >= 128 ? 128 : 64;
-  return bf16 ? cuda_status(launch_pdl(split_reduce_kernel<__nv_bfloat16>, rgrid, dim3(threads), 0,
-                                       stream, rp))
-              : cuda_status(launch_pdl(split_reduce_kernel<__half>, rgrid, dim3(threads), 0,
-                                       stream, rp));
+  return paged_decode_impl(&t, c->seq_prefix_pages, pl.chunks, cuda_stream);
 }

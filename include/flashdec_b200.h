@@ -158,29 +158,30 @@ int fd_paged_decode(const fd_paged_decode_args* args, void* cuda_stream);
  * sequences share the first pages of their block-table rows (a prompt prefix
  * registered once and attached to every member: flashdec/cache.py:192-276).
  * The shared pages are read once per KV head for all of a group's query rows
- * (prefix pass, 64 rows per CTA), the rest of every sequence by the split
- * decode (tail pass), and the split reducer merges both (LSE merge of
- * flashdec/kernels/paged_decode.py:593-635): three launches on the stream.
- * args->num_splits, epilogue and part_* are ignored; args->scratch must hold
- * fd_cascade_workspace bytes.  Every member's seq_len must exceed its
- * group's prefix tokens (the current token is private).  Requires caches that
- * the TMA loader can address (token- or dim-major pages); FD_ERR_UNSUPPORTED
- * otherwise (call fd_paged_decode instead). */
+ * (prefix pass, 128 rows per CTA, one partial per chunk of pages); the rest of
+ * every sequence goes through the split decode (tail pass), whose last CTA
+ * per (sequence, head block) merges the split partials and the member's
+ * prefix partials (LSE merge of flashdec/kernels/paged_decode.py:593-635).
+ * Two launches on the stream.  args->num_splits, epilogue and part_* are
+ * ignored; args->scratch and args->tickets must hold fd_cascade_workspace's
+ * sizes (tickets zero-filled once; the kernels leave them zero).  The group
+ * description lives in HOST memory and is copied into the launch; every
+ * member's seq_len must exceed its group's prefix tokens (its current token
+ * is private).  FD_ERR_UNSUPPORTED for caches the TMA loader cannot address
+ * or more than 32 groups / 512 members (call fd_paged_decode instead). */
 typedef struct fd_cascade_args {
   int32_t struct_size;             /* = sizeof(fd_cascade_args) */
-  int32_t num_groups;              /* >= 1 */
-  const int32_t* group_start;      /* [num_groups + 1] CSR offsets into group_members */
-  const int32_t* group_members;    /* sequence indices (rows of q), grouped */
-  const int32_t* group_pages;      /* [num_groups] shared pages; pages * block_size % 32 == 0 */
-  const int32_t* seq_prefix_pages; /* [num_seqs] the sequence's group_pages, 0 outside groups */
-  int32_t max_group_members;       /* host-side bound: largest group */
-  int32_t max_prefix_tiles;        /* host-side bound: largest group_pages * block_size / 32 */
-  int32_t chunks;                  /* prefix chunks per (group, kv head, 64 rows); 0: auto */
+  int32_t num_groups;              /* 1..32 */
+  const int32_t* group_start;      /* host [num_groups + 1]: CSR offsets into group_members */
+  const int32_t* group_members;    /* host: sequence indices (rows of q), grouped, <= 512 */
+  const int32_t* group_pages;      /* host [num_groups]: shared pages, pages * block_size % 32 == 0 */
+  const int32_t* seq_prefix_pages; /* DEVICE [num_seqs]: the sequence's group_pages, 0 outside */
+  int32_t chunks;                  /* prefix chunks per (group, kv head, 128 rows); 0: auto */
   int32_t tail_splits;             /* splits of every sequence's tail; 0: auto */
 } fd_cascade_args;
 
 int fd_cascade_workspace(const fd_paged_decode_args* args, const fd_cascade_args* cascade,
-                         size_t* scratch_bytes);
+                         size_t* scratch_bytes, int64_t* tickets_needed);
 int fd_cascade_decode(const fd_paged_decode_args* args, const fd_cascade_args* cascade,
                       void* cuda_stream);
 

@@ -6,7 +6,7 @@ restatement of flashdec/paged_reference.py:19-125) gives for the full
 sequences: the prefix pass attends the shared leading pages of each group,
 the tail pass the rest, and the split reducer merges them.  Cases cover one
 and several groups, sequences outside any group, page sizes 8/16/32, head_dim
-64/128, GQA groups 1..16 (so 1..3 row blocks of 64 query rows), more chunks
+64/128, GQA groups 1..16 (1 or 2 row blocks of 128 query rows), more chunks
 than prefix tiles (empty chunks), fp16/bf16, and the engine's fused append
 with RoPE (cache bytes identical to the plain fused launch)."""
 

@@ -206,6 +206,58 @@ def test_shared_prefix_engine_matches_oracle():
     assert cache.metrics()["active_prefix_references"] == 2
 
 
+@pytest.mark.parametrize("bs,nb", [(32, 8), (16, 12)])
+def test_shared_prefix_cascade_engine_matches_oracle(bs, nb, monkeypatch):
+    """Rows sharing a registered prefix of >= 128 tokens take the cascade
+    path (prefix pass + tail pass + merge); outputs against the oracle over
+    the full histories, cache contents exact."""
+    from flashdec_b200 import DecodeEngine, PagedKVCache
+
+    monkeypatch.setenv("FLASHDEC_B200_CASCADE", "1")  # the engine's opt-in
+    L, hq, hkv, d, dtype = 2, 16, 2, 128, "bfloat16"
+    rng = np.random.default_rng(15)
+    cache = PagedKVCache(L, hkv, d, bs, max_blocks=96, dtype=torch.bfloat16, device="cuda",
+                         prefix_cache_capacity_blocks=nb)
+    eng = DecodeEngine(cache, append_backend="fused_cuda")
+    pk = _normal(rng, (L, nb, hkv, bs, d), dtype)
+    pv = _normal(rng, (L, nb, hkv, bs, d), dtype)
+    eng.register_prefix("sys", to_dev(pk, dtype), to_dev(pv, dtype))
+    pk_tok = pk.transpose(0, 1, 3, 2, 4).reshape(L, nb * bs, hkv, d)
+    pv_tok = pv.transpose(0, 1, 3, 2, 4).reshape(L, nb * bs, hkv, d)
+    store = OracleStore(L)
+    ids = ["p1", "solo", "p2", "p3", "p4"]
+    for r in ids:
+        eng.add_request(r)
+    eng.admit()
+    for r in ids:
+        if r == "solo":
+            store.add(r)
+        else:
+            cache.attach_prefix(r, "sys")
+            store.add(r, pk_tok, pv_tok)
+    table = _table(96, 1e6)
+    for step in range(45):
+        tx = eng.begin_step(ids)
+        assert cache._cascades.groups is not None  # the cascade path is taken
+        pos = tx.positions.cpu().numpy()
+        for layer in range(L):
+            q = _normal(rng, (len(ids), hq, d), dtype)
+            k = _normal(rng, (len(ids), hkv, d), dtype)
+            v = _normal(rng, (len(ids), hkv, d), dtype)
+            res = eng.step_layer(tx, layer, to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype),
+                                 rotary_dim=96, base=1e6)
+            q_rot = apply_rope_ref(q, pos, 96, 1e6, dtype, table)
+            k_rot = apply_rope_ref(k, pos, 96, 1e6, dtype, table)
+            for i, r in enumerate(ids):
+                store.k[r][layer].append(k_rot[i])
+                store.v[r][layer].append(np.asarray(v[i], np.float32))
+            assert_attention_close(to_np(res.output), store.attention(layer, ids, q_rot))
+        eng.commit_step(tx)
+    np.testing.assert_array_equal(
+        to_np(cache.k_cache[:, list(cache.prefix_state("sys")["block_ids"])]), pk)
+    _check_cache_contents(cache, store, ids, dtype)
+
+
 def test_single_layer_step_backends_agree_bitwise():
     from flashdec_b200 import DecodeEngine, PagedKVCache
 

@@ -119,11 +119,15 @@ def test_rope_fields_are_validated():
                              rope=(63, invf, pos), **kw)
 
 
-def test_engine_transaction_one_launch_matches_two_launch_backend():
+def test_engine_transaction_one_launch_matches_two_launch_backend(monkeypatch):
     """DecodeEngine with append_backend='fused_cuda' (one launch per layer)
     and 'torch' (RoPE + append launch, then decode) on the same inputs,
-    with a shared prefix: identical outputs and caches."""
+    with a shared prefix: identical outputs and caches.  (The cascade path,
+    which sums in another order, is off here; tests/test_engine_gpu.py checks
+    it against the oracle.)"""
     from flashdec_b200 import DecodeEngine, PagedKVCache
+
+    monkeypatch.setenv("FLASHDEC_B200_CASCADE", "0")
 
     L, hq, hkv, d, bs = 3, 16, 2, 128, 32
     results = {}
