@@ -613,9 +613,10 @@ def run_c5(torch, device, args, num_layers=36, num_requests=16, prefix_tokens=40
             "steps": steps, "us_per_step_wall": wall_us, "us_per_step_device_span": dev_us,
             "tokens_per_s": num_requests / (wall_us * 1e-6),
             "us_per_layer_wall": wall_us / num_layers,
-            "gpu_launches_per_step": 2 * num_layers,
+            "gpu_launches_per_step": num_layers,  # one fused RoPE + append + decode per layer
             "logical_kv_bytes_per_step": logical, "unique_kv_bytes_per_step": unique,
-            "note": "host-driven (Python engine per layer, no graph capture)"}
+            "note": "host-driven (Python engine per layer, no graph capture); one launch per "
+                    "layer (RoPE + K/V store + decode)"}
 
 
 def run_sweep(torch, device, stream):
