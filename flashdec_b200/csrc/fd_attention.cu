@@ -163,6 +163,17 @@ __device__ __forceinline__ uint32_t stage_row_base(int row, int half) {
     return half * (kTile * 128) + row * 128;
   }
 }
+// Byte distance of 16 tile rows and of one 64-dim half in a stage, for the
+// per-lane ldmatrix offsets that are hoisted out of the tile loop: row
+// r + 16 np of half h of chunk (8 h + c8) sits at
+//   stage_row_base(r, 0) + np * kRows16Bytes + h * kHalfStride + ((c8 ^ (r % 8)) << 4)
+// for r < 16 (a multiple-of-8 row shift keeps r % 8, hence the swizzle).
+template <int kPageRows>
+struct StageStrides {
+  static constexpr uint32_t kRows16Bytes = kPageRows > 0 ? (16 / kPageRows) * (kPageRows * 256) : 16 * 128;
+  static constexpr uint32_t kHalfStride = kPageRows > 0 ? kPageRows * 128 : kTile * 128;
+};
+
 template <int kPageRows>
 __device__ __forceinline__ uint32_t stage_tile_offset(int row, int dim) {
   const int dd = dim & 63;
@@ -733,6 +744,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t4 = lane & 3;   // thread in group
   const int mi = lane >> 3;  // ldmatrix matrix index
   const int r8 = lane & 7;   // ldmatrix row
+  // Per-lane ldmatrix offsets, the same for every tile (StageStrides): K
+  // rows (mi >> 1) * 8 + r8 with chunk 2 j + (mi & 1) of a half, V rows
+  // (mi & 1) * 8 + r8 with chunk 2 j + (mi >> 1).
+  using SS = StageStrides<kPageRows>;
+  const uint32_t k_lane = stage_row_base<kPageRows>((mi >> 1) * 8 + r8, 0);
+  const uint32_t v_lane = stage_row_base<kPageRows>((mi & 1) * 8 + r8, 0);
+  uint32_t k_sw[4], v_sw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    k_sw[j] = k_lane + ((((2 * j) + (mi & 1)) ^ r8) << 4);
+    v_sw[j] = v_lane + ((((2 * j) + (mi >> 1)) ^ r8) << 4);
+  }
   int cst = 0;        // (stage, phase parity) of the next tile
   uint32_t cph = 0;
   // ---- Q fragments (A operand, rows = query heads of the head block) ----
@@ -934,10 +957,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < D / 16; ++ks) {
 #pragma unroll
         for (int np = 0; np < 2; ++np) {
-          const int tok = np * 16 + (mi >> 1) * 8 + r8;
-          const int chunk = ks * 2 + (mi & 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4(kbase + stage_chunk_offset<kPageRows>(tok, chunk), b0a, b1a, b0b, b1b);
+          ldsm_x4(kbase + k_sw[ks & 3] + np * SS::kRows16Bytes + (ks >> 2) * SS::kHalfStride, b0a,
+                  b1a, b0b, b1b);
           mma_16816<T>(sacc[2 * np], qf[ks], b0a, b1a);
           mma_16816<T>(sacc[2 * np + 1], qf[ks], b0b, b1b);
         }
@@ -945,18 +967,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- online softmax (base 2, scale folded in) ----
       float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (vmask == 0xffffffffu) {  // a full tile: no masking
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 4; ++j) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int tok = 8 * j + 2 * t4 + e;
-          const bool valid = (vmask >> tok) & 1u;
-          const float x0 = valid ? sacc[j][e] * p.scale_log2 : -INFINITY;
-          const float x1 = valid ? sacc[j][2 + e] * p.scale_log2 : -INFINITY;
-          sacc[j][e] = x0;
-          sacc[j][2 + e] = x1;
-          mx0 = fmaxf(mx0, x0);
-          mx1 = fmaxf(mx1, x1);
+          for (int e = 0; e < 4; ++e) sacc[j][e] *= p.scale_log2;
+          mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
+          mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int tok = 8 * j + 2 * t4 + e;
+            const bool valid = (vmask >> tok) & 1u;
+            const float x0 = valid ? sacc[j][e] * p.scale_log2 : -INFINITY;
+            const float x1 = valid ? sacc[j][2 + e] * p.scale_log2 : -INFINITY;
+            sacc[j][e] = x0;
+            sacc[j][2 + e] = x1;
+            mx0 = fmaxf(mx0, x0);
+            mx1 = fmaxf(mx1, x1);
+          }
         }
       }
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -983,12 +1015,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       l1 = l1 * alpha1 + ps1;
       m0 = mn0;
       m1 = mn1;
+      // Once the running maxima settle (alpha == 1: exactly the old max) the
+      // rescale multiplies by 1.0; skipping it changes no bit.
+      if (!__all_sync(0xffffffffu, alpha0 == 1.f && alpha1 == 1.f)) {
 #pragma unroll
-      for (int j = 0; j < D / 8; ++j) {
-        o[j][0] *= alpha0;
-        o[j][1] *= alpha0;
-        o[j][2] *= alpha1;
-        o[j][3] *= alpha1;
+        for (int j = 0; j < D / 8; ++j) {
+          o[j][0] *= alpha0;
+          o[j][1] *= alpha0;
+          o[j][2] *= alpha1;
+          o[j][3] *= alpha1;
+        }
       }
 
       // ---- O += P V ----
@@ -1001,10 +1037,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         a[3] = pack2<T>(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
 #pragma unroll
         for (int dp = 0; dp < D / 16; ++dp) {
-          const int tok = kk * 16 + (mi & 1) * 8 + r8;
-          const int chunk = dp * 2 + (mi >> 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4_t(vbase + stage_chunk_offset<kPageRows>(tok, chunk), b0a, b1a, b0b, b1b);
+          ldsm_x4_t(vbase + v_sw[dp & 3] + kk * SS::kRows16Bytes + (dp >> 2) * SS::kHalfStride,
+                    b0a, b1a, b0b, b1b);
           mma_16816<T>(o[2 * dp], a, b0a, b1a);
           mma_16816<T>(o[2 * dp + 1], a, b0b, b1b);
         }
@@ -1873,6 +1908,8 @@ Plan make_plan(const fd_paged_decode_args& a, const Derived& dv, const DeviceInf
     return pl;
   }
   pl.splits = 0;
+  // Two resident CTAs per SM when a ring of at least 4 stages fits in half
+  // an SM's shared memory next to the schedule tables.
   const int g = a.max_ctas > 0 ? a.max_ctas : dev.num_sms;
   pl.grid = g < 1 ? 1 : g;
   return pl;
