@@ -42,6 +42,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <type_traits>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -1817,6 +1818,352 @@ __global__ void __launch_bounds__(kPrefixThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// shared-prefix pass on the 5th-generation tensor cores (tcgen05 / UMMA)
+// ---------------------------------------------------------------------------
+// Same work unit and output as prefix_kernel, for head_dim 128 and 32-token
+// pages: CTA (chunk, 128-row block, group x KV head) holds the chunk's n <= 8
+// tiles in shared memory -- K and V each as one [half][256 tokens][64 dims]
+// operand (TMA, 128B swizzle; tile i at token 32 i) -- and its 128 query rows
+// (K-major, 128B swizzle), one TMEM lane per row.
+//   1. one thread issues S = Q K^T for the whole chunk (M 128, N 32 n, K 128:
+//      8 UMMAs) into TMEM columns [0, 32 n);
+//   2. each consumer thread (one row) takes its row max over the chunk's
+//      scores, then P = exp2(S - max) (no online rescale needed), and writes P
+//      as bf16 over K (no longer needed; core-matrix layout, K-major);
+//   3. the thread issues O = P V (M 128, N 128, K 32 n: 2 n UMMAs, V as the
+//      MN-major operand) into TMEM columns [256, 384);
+//   4. O goes through shared memory to coalesced row writes of the
+//      (max, sum, acc) partial.
+constexpr int kUmmaMaxTiles = 8;
+constexpr int kUmmaMaxMembers = 33;  // RoPE table rows (members of one 128-row block, group >= 4)
+constexpr int kUmmaQBytes = 2 * 128 * 128;  // [half][128 rows][128 B]
+constexpr int kUmmaTmemCols = 512;
+constexpr int kUmmaOCol = 256;
+constexpr int kUmmaKBytes = 2 * kUmmaMaxTiles * kTile * 128;  // [half][256 tokens][128 B]
+
+constexpr size_t prefix_umma_smem_bytes() {
+  return 1024 + kUmmaQBytes + static_cast<size_t>(kUmmaMaxTiles) * Smem<128>::kStageBytes +
+         kUmmaMaxMembers * 128 * sizeof(float) + 2 * 128 * sizeof(int) + 16 * sizeof(uint64_t) +
+         64;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefix_umma_kernel(const __grid_constant__ PrefixParams p,
+                       const __grid_constant__ CUtensorMap tmap_k,
+                       const __grid_constant__ CUtensorMap tmap_v) {
+  constexpr int D = 128;
+  using SM = Smem<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* qsm = smem;
+  uint8_t* tiles = qsm + kUmmaQBytes;  // K operand, then V operand (kUmmaKBytes each)
+  uint8_t* kreg = tiles;
+  uint8_t* vreg = tiles + kUmmaKBytes;
+  float* rtab = reinterpret_cast<float*>(tiles + kUmmaMaxTiles * SM::kStageBytes);
+  int* row_seq = reinterpret_cast<int*>(rtab + kUmmaMaxMembers * 128);
+  int* row_pos = row_seq + 128;  // unused slot kept for alignment of the barriers
+  uint64_t* bars = reinterpret_cast<uint64_t*>(row_pos + 128);
+  uint64_t* full_bar = bars;                     // every tile of the chunk landed (TMA bytes)
+  uint64_t* q_ready = bars + kUmmaMaxTiles;      // Q staged (consumer arrivals)
+  uint64_t* s_done = q_ready + 1;                // S UMMAs complete (commit)
+  uint64_t* p_ready = s_done + 1;                // P written (consumer arrivals)
+  uint64_t* o_done = p_ready + 1;                // PV UMMAs complete (commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  int* misc = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  volatile int* abort_flag = misc;
+
+  if (tid == 0) {
+    mbar_init(smem_u32(full_bar), 1);
+    mbar_init(smem_u32(q_ready), kConsumerThreads);
+    mbar_init(smem_u32(s_done), 1);
+    mbar_init(smem_u32(p_ready), kConsumerThreads);
+    mbar_init(smem_u32(o_done), 1);
+    fence_mbar_init();
+    misc[0] = 0;
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tmem_slot), kUmmaTmemCols);
+  if (warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  const int c = static_cast<int>(blockIdx.x);
+  const int row0 = static_cast<int>(blockIdx.y) * 128;
+  const int g = static_cast<int>(blockIdx.z) / p.num_kv_heads;
+  const int h = static_cast<int>(blockIdx.z) - g * p.num_kv_heads;
+  const int m0 = p.grp_start[g];
+  const int rows = (p.grp_start[g + 1] - m0) * p.group;
+  const int tiles_all = p.grp_pages[g] * p.block_size / kTile;
+  const int t0 = static_cast<int>(static_cast<int64_t>(c) * tiles_all / p.chunks);
+  const int t1 = static_cast<int>(static_cast<int64_t>(c + 1) * tiles_all / p.chunks);
+  const int nt = min(t1 - t0, kUmmaMaxTiles);  // the host keeps chunks <= 8 tiles
+  const bool active = row0 < rows;
+
+  if (active && warp == kConsumerWarps) {
+    // ======== producer (TMA, lane i: tile t0 + i) and UMMA issue (lane 0) ========
+    const int rep = p.grp_members[m0];
+    const uint64_t policy = l2_policy_evict_first();
+    bool bad = false;
+    int blk = -1;
+    if (lane < nt) {
+      const int64_t lb = t0 + lane;  // 32-token pages: page = tile
+      blk = lb < p.max_blocks ? static_cast<int>(load_index(
+                                    p.bt, p.bt64, static_cast<int64_t>(rep) * p.bts0 + lb * p.bts1))
+                              : -1;
+    }
+    const bool valid = lane < nt && blk >= 0 && blk < p.num_blocks;
+    bad = lane < nt && !valid;
+    const uint32_t nvalid = __popc(__ballot_sync(0xffffffffu, valid));
+    // one barrier for the chunk; the byte count is posted before any copy
+    if (lane == 0) mbar_arrive_expect_tx(smem_u32(full_bar), nvalid * SM::kStageBytes);
+    __syncwarp();
+    if (valid) {
+#pragma unroll
+      for (int op = 0; op < 4; ++op) {
+        const int plane = op >> 1;
+        const int hh = op & 1;
+        const int* perm = plane ? p.vperm : p.kperm;
+        tma_load_4d(smem_u32((plane ? vreg : kreg) + hh * (kUmmaKBytes / 2) + lane * SM::kHalfBytes),
+                    plane ? &tmap_v : &tmap_k, smem_u32(full_bar), hh * 64,
+                    tmap_coord(perm[0], h, blk), tmap_coord(perm[1], h, blk),
+                    tmap_coord(perm[2], h, blk), policy);
+      }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+    if (lane == 0) {
+      const uint32_t id_s = umma_idesc_f16(kBf16, false, 128, 32 * max(nt, 1));
+      constexpr uint32_t kIdO = umma_idesc_f16(kBf16, true, 128, 128);
+      bool ok = mbar_wait(smem_u32(q_ready), 0u, p.status, abort_flag);
+      ok = ok && mbar_wait(smem_u32(full_bar), 0u, p.status, abort_flag);
+      tc_fence_after();
+      const uint32_t qbase = smem_u32(qsm);
+      const uint32_t kbase = smem_u32(kreg);
+      if (ok && nt > 0) {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {  // S = Q K^T over the chunk (N = 32 nt)
+          const uint32_t koff = (k & 3) * 32u;
+          const uint64_t a = umma_smem_desc(qbase + (k >> 2) * (kUmmaQBytes / 2) + koff, 16, 1024, 2);
+          const uint64_t b = umma_smem_desc(kbase + (k >> 2) * (kUmmaKBytes / 2) + koff, 16, 1024, 2);
+          umma_f16(taddr, a, b, id_s, k > 0);
+        }
+      }
+      umma_commit(smem_u32(s_done));  // also when nothing was issued: the waiters go on
+      ok = ok && mbar_wait(smem_u32(p_ready), 0u, p.status, abort_flag);
+      tc_fence_after();
+      const uint32_t vbase = smem_u32(vreg);
+      for (int kk = 0; ok && kk < 2 * nt; ++kk) {  // O = P V, 16 tokens per UMMA
+        const uint64_t a = umma_smem_desc(kbase + kk * 256, 128, 4096, 0);   // P over K
+        const uint64_t b = umma_smem_desc(vbase + kk * 2048, kUmmaKBytes / 2, 1024, 2);
+        umma_f16(taddr + kUmmaOCol, a, b, kIdO, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(smem_u32(o_done));
+    }
+    __syncwarp();
+  } else if (active) {
+    // ======== consumers: thread = query row = TMEM lane ========
+    const int r = tid;  // warps 0-3 -> rows 0-127 -> TMEM lanes 0-127
+    const int gr = row0 + r;
+    int seq = -1, qh = 0, mem = 0;
+    if (gr < rows) {
+      mem = gr / p.group;
+      seq = p.grp_members[m0 + mem];
+      qh = h * p.group + (gr - mem * p.group);
+    }
+    row_seq[r] = seq;
+    // RoPE table: cos / sin per (member of this block, pair index)
+    const int half = p.rope_dim >> 1;
+    const int mem_first = row0 / p.group;
+    const int nmem = min((row0 + 127) / p.group, p.grp_start[g + 1] - m0 - 1) - mem_first + 1;
+    const bool table = p.rope_dim > 0 && nmem <= kUmmaMaxMembers;
+    if (table) {
+      for (int e = tid; e < nmem * half; e += kConsumerThreads) {
+        const int mm = e / half;
+        const int i = e - mm * half;
+        const int sq = p.grp_members[m0 + mem_first + mm];
+        const float posf = static_cast<float>(
+            load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(sq) * p.rope_pos_stride));
+        float sn, cs;
+        sincosf(__fmul_rn(posf, p.rope_inv_freq[i]), &sn, &cs);
+        rtab[mm * 128 + i] = cs;
+        rtab[mm * 128 + 64 + i] = sn;
+      }
+      named_barrier(kBarConsumers, kConsumerThreads);
+    }
+    // ---- Q rows into the K-major 128B-swizzled operand: coalesced 16-byte
+    // chunks, then RoPE in place (pairs (i, i + rope_dim / 2) of a row) ----
+    auto q_chunk = [&](int row, int cc) -> uint8_t* {
+      return qsm + (cc >> 3) * (kUmmaQBytes / 2) + row * 128 + (((cc & 7) ^ (row & 7)) << 4);
+    };
+    {
+      // 16 chunks per thread (2048 / 128): every load is issued before the
+      // first store, so the staging costs one memory round trip
+      constexpr int kPer = 128 * (D / 8) / kConsumerThreads;
+      uint4 v[kPer];
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int e = tid + k * kConsumerThreads;
+        const int rr = e / (D / 8);
+        const int cc = e - rr * (D / 8);
+        const int grr = row0 + rr;
+        v[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (grr < rows) {
+          const int mm = grr / p.group;
+          const int sq = p.grp_members[m0 + mm];
+          const int hq = h * p.group + (grr - mm * p.group);
+          const T* src = static_cast<const T*>(p.q) + sq * p.qs0 + hq * p.qs1 + cc * 8 * p.qs2;
+          if (p.qs2 == 1 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+            v[k] = __ldg(reinterpret_cast<const uint4*>(src));
+          } else {
+            __align__(16) T el[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) el[i] = src[i * p.qs2];
+            v[k] = *reinterpret_cast<const uint4*>(el);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int e = tid + k * kConsumerThreads;
+        const int rr = e / (D / 8);
+        *reinterpret_cast<uint4*>(q_chunk(rr, e - rr * (D / 8))) = v[k];
+      }
+    }
+    if (p.rope_dim > 0) {
+      named_barrier(kBarConsumers, kConsumerThreads);
+      for (int e = tid; e < 128 * half; e += kConsumerThreads) {
+        const int rr = e / half;
+        const int i = e - rr * half;
+        const int grr = row0 + rr;
+        if (grr >= rows) continue;
+        const int mm = grr / p.group;
+        float cs, sn;
+        if (table) {
+          cs = rtab[(mm - mem_first) * 128 + i];
+          sn = rtab[(mm - mem_first) * 128 + 64 + i];
+        } else {
+          const int sq = p.grp_members[m0 + mm];
+          const float posf = static_cast<float>(
+              load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(sq) * p.rope_pos_stride));
+          sincosf(__fmul_rn(posf, p.rope_inv_freq[i]), &sn, &cs);
+        }
+        T* x1p = reinterpret_cast<T*>(q_chunk(rr, i >> 3) + (i & 7) * 2);
+        T* x2p = reinterpret_cast<T*>(q_chunk(rr, (i + half) >> 3) + ((i + half) & 7) * 2);
+        float y1, y2;
+        rope_rotate_pair_cs(to_f32<T>(*x1p), to_f32<T>(*x2p), cs, sn, y1, y2);
+        *x1p = from_f32<T>(y1);
+        *x2p = from_f32<T>(y2);
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(smem_u32(q_ready));
+
+    // ---- scores -> row max -> P (bf16) over the K area of each tile ----
+    // tcgen05.ld is warp-collective (.sync.aligned): every TMEM load below
+    // runs on all 32 lanes under warp-uniform conditions; only the global
+    // writes depend on the row.
+    const uint32_t lane_addr = taddr + (static_cast<uint32_t>(warp * 32) << 16);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(s_done), 0u, p.status, abort_flag));
+    tc_fence_after();
+    float mrow = -INFINITY, lrow = 0.f;
+    if (ok && nt > 0) {
+      for (int i = 0; i < nt; ++i) {
+        float v[32];
+        tmem_ld32(lane_addr + 32 * i, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mrow = fmaxf(mrow, v[j] * p.scale_log2);
+      }
+      // P in the no-swizzle K-major core-matrix layout over the K operand:
+      // row r, tokens 8 k .. 8 k + 7 at (r / 8) * 4096 + k * 128 + (r % 8) * 16
+      for (int i = 0; i < nt; ++i) {
+        float v[32];
+        tmem_ld32(lane_addr + 32 * i, v);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {  // tokens 32 i + 8 cc .. + 7
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float a0 = exp2f(v[8 * cc + 2 * e] * p.scale_log2 - mrow);
+            const float a1 = exp2f(v[8 * cc + 2 * e + 1] * p.scale_log2 - mrow);
+            lrow += a0 + a1;
+            w[e] = pack2<T>(a0, a1);
+          }
+          *reinterpret_cast<uint4*>(kreg + (r >> 3) * 4096 + (4 * i + cc) * 128 + (r & 7) * 16) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(smem_u32(p_ready));
+
+    // ---- this row's (max, sum, acc) partial ----
+    ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), 0u, p.status, abort_flag)) && ok;
+    tc_fence_after();
+    {
+      // O rows go through shared memory (the tile area: the PV UMMAs that read
+      // it have completed) so that each warp writes whole 512-byte rows.
+      // Row r's 16-byte chunk k sits at r * 512 + ((k ^ (r % 32)) * 16): the
+      // XOR spreads a warp's same-chunk writes over all banks.
+      float* ob = reinterpret_cast<float*>(tiles);
+      for (int j = 0; j < 4; ++j) {
+        float v[32];
+        if (ok && nt > 0) {
+          tmem_ld32(lane_addr + kUmmaOCol + 32 * j, v);  // all lanes
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const int k = (32 * j + e) >> 2;
+          *reinterpret_cast<float4*>(ob + r * 128 + ((k ^ (r & 31)) << 2)) =
+              make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        }
+      }
+      const int slot = p.slot0 + c;
+      if (seq >= 0) {
+        const int64_t so = seq * p.pss0 + qh * p.pss1 + slot * p.pss2;
+        const bool empty = !(ok && nt > 0);
+        p.pmax[so] = (empty || mrow == -INFINITY) ? -INFINITY : mrow * kLn2;  // natural-log units
+        p.psum[so] = empty ? 0.f : lrow;
+      }
+      named_barrier(kBarConsumers, kConsumerThreads);
+      // warp w writes rows w, w + 4, ...: lane l moves 16-byte chunk l
+      for (int rr = warp; rr < 128; rr += kConsumerWarps) {
+        const int sq = row_seq[rr];
+        if (sq < 0) continue;  // warp-uniform (one row per iteration)
+        const int grr = row0 + rr;
+        const int hq = h * p.group + (grr - (grr / p.group) * p.group);
+        float* acc = p.pacc + sq * p.pas0 + hq * p.pas1 + slot * p.pas2;
+        const float4 val = *reinterpret_cast<const float4*>(ob + rr * 128 + ((lane ^ (rr & 31)) << 2));
+        if (p.pas3 == 1 && (reinterpret_cast<uintptr_t>(acc) & 15u) == 0) {
+          reinterpret_cast<float4*>(acc)[lane] = val;
+        } else {
+          acc[(4 * lane) * p.pas3] = val.x;
+          acc[(4 * lane + 1) * p.pas3] = val.y;
+          acc[(4 * lane + 2) * p.pas3] = val.z;
+          acc[(4 * lane + 3) * p.pas3] = val.w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(taddr, kUmmaTmemCols);
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 namespace {
@@ -2338,6 +2685,7 @@ namespace {
 
 struct CascadePlan {
   int chunks, splits, row_blocks;
+  bool umma;  // prefix pass on tcgen05 (head_dim 128, 32-token pages)
 };
 
 // Host checks of the group description (it is copied into the prefix
@@ -2379,6 +2727,7 @@ CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c
   }
   const int64_t rows = static_cast<int64_t>(max_members) * dv.group;
   pl.row_blocks = static_cast<int>((rows + kPrefixRows - 1) / kPrefixRows);
+  pl.umma = a.head_dim == 128 && a.block_size == 32 && prefix_umma_enabled();
   const int64_t units = static_cast<int64_t>(c.num_groups) * a.num_kv_heads * pl.row_blocks;
   if (c.chunks > 0) {
     pl.chunks = c.chunks;
@@ -2387,6 +2736,10 @@ CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c
     int64_t ch = (dev.num_sms + units - 1) / units;
     ch = std::min<int64_t>(ch, std::max(1, max_tiles / 2));
     pl.chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ch, 32)));
+  }
+  if (pl.umma) {
+    // a UMMA prefix CTA holds its whole chunk in shared memory
+    pl.chunks = std::max(pl.chunks, (max_tiles + kUmmaMaxTiles - 1) / kUmmaMaxTiles);
   }
   if (c.tail_splits > 0) {
     pl.splits = c.tail_splits;
@@ -2416,6 +2769,23 @@ int launch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensor
   });
   if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
   return cuda_status(launch_pdl(kern, grid, dim3(kPrefixThreads), smem, stream, prm, mk, mv));
+}
+
+template <typename T>
+int launch_prefix_umma(const PrefixParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
+                       dim3 grid, const DeviceInfo& dev, cudaStream_t stream) {
+  auto kern = prefix_umma_kernel<T>;
+  const size_t smem = prefix_umma_smem_bytes();
+  if (smem > static_cast<size_t>(dev.max_smem_optin)) return FD_ERR_UNSUPPORTED;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  const int slot = dev.device & 63;
+  std::call_once(once[slot], [&] {
+    attr_err[slot] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+  });
+  if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
+  return cuda_status(launch_pdl(kern, grid, dim3(kThreads), smem, stream, prm, mk, mv));
 }
 
 template <typename T, int D>
@@ -2535,7 +2905,10 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   const dim3 pgrid(static_cast<unsigned>(pl.chunks), static_cast<unsigned>(pl.row_blocks),
                    static_cast<unsigned>(c->num_groups * a->num_kv_heads));
   const bool bf16 = a->dtype == FD_DTYPE_BF16;
-  if (D == 128) {
+  if (pl.umma && pp.kperm[3] < 0) {
+    rc = bf16 ? launch_prefix_umma<__nv_bfloat16>(pp, mk, mv, pgrid, *dev, stream)
+              : launch_prefix_umma<__half>(pp, mk, mv, pgrid, *dev, stream);
+  } else if (D == 128) {
     rc = bf16 ? dispatch_prefix<__nv_bfloat16, 128>(pp, mk, mv, pgrid, psmem, *dev, stream)
               : dispatch_prefix<__half, 128>(pp, mk, mv, pgrid, psmem, *dev, stream);
   } else {

@@ -121,6 +121,14 @@ bool cluster_enabled() {
   return on;
 }
 
+bool prefix_umma_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLASHDEC_B200_PREFIX_UMMA");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return FD_OK;
   g_last_cuda_error = cudaGetErrorString(e);

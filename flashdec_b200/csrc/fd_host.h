@@ -59,6 +59,11 @@ bool pdl_enabled();
 // global-memory ticket merge).
 bool cluster_enabled();
 
+// Whether the cascade prefix pass runs on tcgen05 UMMA where it can (head_dim
+// 128, 32-token pages; default on; FLASHDEC_B200_PREFIX_UMMA=0 keeps the
+// mma.sync prefix kernel).
+bool prefix_umma_enabled();
+
 // Launch `kern` with the programmatic-stream-serialization attribute (the
 // kernel calls griddepcontrol.wait before touching global memory).
 template <typename... KArgs, typename... Args>
