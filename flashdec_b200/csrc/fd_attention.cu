@@ -1843,8 +1843,8 @@ constexpr int kUmmaKBytes = 2 * kUmmaMaxTiles * kTile * 128;  // [half][256 toke
 
 constexpr size_t prefix_umma_smem_bytes() {
   return 1024 + kUmmaQBytes + static_cast<size_t>(kUmmaMaxTiles) * Smem<128>::kStageBytes +
-         kUmmaMaxMembers * 128 * sizeof(float) + 2 * 128 * sizeof(int) + 16 * sizeof(uint64_t) +
-         64;
+         kUmmaMaxMembers * 128 * sizeof(float) + 2 * 128 * sizeof(int64_t) +
+         4 * 128 * sizeof(int) + 16 * sizeof(uint64_t) + 64;
 }
 
 template <typename T>
@@ -1863,9 +1863,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* kreg = tiles;
   uint8_t* vreg = tiles + kUmmaKBytes;
   float* rtab = reinterpret_cast<float*>(tiles + kUmmaMaxTiles * SM::kStageBytes);
-  int* row_seq = reinterpret_cast<int*>(rtab + kUmmaMaxMembers * 128);
-  int* row_pos = row_seq + 128;  // unused slot kept for alignment of the barriers
-  uint64_t* bars = reinterpret_cast<uint64_t*>(row_pos + 128);
+  int64_t* row_qoff = reinterpret_cast<int64_t*>(rtab + kUmmaMaxMembers * 128);  // q element
+  int64_t* row_ooff = row_qoff + 128;  // partial acc element offset of the row
+  int* row_seq = reinterpret_cast<int*>(row_ooff + 128);  // -1: padding row
+  float* row_pos = reinterpret_cast<float*>(row_seq + 128);  // RoPE position
+  int* row_mm = reinterpret_cast<int*>(row_pos + 128);  // RoPE table row (member - first)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(row_mm + 128);  // 8-byte aligned: 2 KB + 2 KB above
   uint64_t* full_bar = bars;                     // every tile of the chunk landed (TMA bytes)
   uint64_t* q_ready = bars + kUmmaMaxTiles;      // Q staged (consumer arrivals)
   uint64_t* s_done = q_ready + 1;                // S UMMAs complete (commit)
@@ -1974,17 +1977,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (active) {
     // ======== consumers: thread = query row = TMEM lane ========
     const int r = tid;  // warps 0-3 -> rows 0-127 -> TMEM lanes 0-127
-    const int gr = row0 + r;
-    int seq = -1, qh = 0, mem = 0;
-    if (gr < rows) {
-      mem = gr / p.group;
-      seq = p.grp_members[m0 + mem];
-      qh = h * p.group + (gr - mem * p.group);
-    }
-    row_seq[r] = seq;
-    // RoPE table: cos / sin per (member of this block, pair index)
+    const int slot = p.slot0 + c;
     const int half = p.rope_dim >> 1;
     const int mem_first = row0 / p.group;
+    int seq_r = -1;     // this thread's row: sequence (-1: padding row)
+    int64_t so_r = 0;   // and (max, sum) element offset
+    {
+      const int gr = row0 + r;
+      int seq = -1, mem = mem_first;
+      int64_t qo = 0, oo = 0;
+      float posf = 0.f;
+      if (gr < rows) {
+        mem = gr / p.group;
+        seq = p.grp_members[m0 + mem];
+        const int qh = h * p.group + (gr - mem * p.group);
+        qo = seq * p.qs0 + qh * p.qs1;
+        oo = seq * p.pas0 + qh * p.pas1 + slot * p.pas2;
+        so_r = seq * p.pss0 + qh * p.pss1 + slot * p.pss2;
+        if (p.rope_dim > 0)
+          posf = static_cast<float>(
+              load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(seq) * p.rope_pos_stride));
+      }
+      row_seq[r] = seq;
+      row_qoff[r] = qo;
+      row_ooff[r] = oo;
+      row_pos[r] = posf;
+      row_mm[r] = mem - mem_first;
+      seq_r = seq;
+    }
+    // RoPE table: cos / sin per (member of this block, pair index)
     const int nmem = min((row0 + 127) / p.group, p.grp_start[g + 1] - m0 - 1) - mem_first + 1;
     const bool table = p.rope_dim > 0 && nmem <= kUmmaMaxMembers;
     if (table) {
@@ -1999,13 +2020,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         rtab[mm * 128 + i] = cs;
         rtab[mm * 128 + 64 + i] = sn;
       }
-      named_barrier(kBarConsumers, kConsumerThreads);
     }
-    // ---- Q rows into the K-major 128B-swizzled operand: coalesced 16-byte
-    // chunks, then RoPE in place (pairs (i, i + rope_dim / 2) of a row) ----
+    named_barrier(kBarConsumers, kConsumerThreads);
+    // ---- Q rows into the K-major 128B-swizzled operand: 16-byte chunks, 16
+    // lanes per row (coalesced), RoPE applied in registers on the way.  With
+    // rope_dim / 2 a multiple of 8, chunk cc < hp (hp = rope_dim / 16) pairs
+    // with chunk cc + hp of the same row, one warp shuffle away. ----
     auto q_chunk = [&](int row, int cc) -> uint8_t* {
       return qsm + (cc >> 3) * (kUmmaQBytes / 2) + row * 128 + (((cc & 7) ^ (row & 7)) << 4);
     };
+    const int hp = (p.rope_dim > 0 && (half & 7) == 0) ? (half >> 3) : 0;
     {
       // 16 chunks per thread (2048 / 128): every load is issued before the
       // first store, so the staging costs one memory round trip
@@ -2013,16 +2037,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint4 v[kPer];
 #pragma unroll
       for (int k = 0; k < kPer; ++k) {
-        const int e = tid + k * kConsumerThreads;
-        const int rr = e / (D / 8);
-        const int cc = e - rr * (D / 8);
-        const int grr = row0 + rr;
+        const int rr = (tid + k * kConsumerThreads) >> 4;
+        const int cc = lane & 15;
         v[k] = make_uint4(0u, 0u, 0u, 0u);
-        if (grr < rows) {
-          const int mm = grr / p.group;
-          const int sq = p.grp_members[m0 + mm];
-          const int hq = h * p.group + (grr - mm * p.group);
-          const T* src = static_cast<const T*>(p.q) + sq * p.qs0 + hq * p.qs1 + cc * 8 * p.qs2;
+        if (row_seq[rr] >= 0) {
+          const T* src = static_cast<const T*>(p.q) + row_qoff[rr] + cc * 8 * p.qs2;
           if (p.qs2 == 1 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
             v[k] = __ldg(reinterpret_cast<const uint4*>(src));
           } else {
@@ -2035,28 +2054,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int k = 0; k < kPer; ++k) {
-        const int e = tid + k * kConsumerThreads;
-        const int rr = e / (D / 8);
-        *reinterpret_cast<uint4*>(q_chunk(rr, e - rr * (D / 8))) = v[k];
+        const int rr = (tid + k * kConsumerThreads) >> 4;
+        const int cc = lane & 15;
+        if (hp > 0) {  // warp-uniform
+          const bool lo = cc < hp;
+          const bool hi = !lo && cc < 2 * hp;
+          const int src = lo ? lane + hp : (hi ? lane - hp : lane);
+          uint4 w;
+          w.x = __shfl_sync(0xffffffffu, v[k].x, src);
+          w.y = __shfl_sync(0xffffffffu, v[k].y, src);
+          w.z = __shfl_sync(0xffffffffu, v[k].z, src);
+          w.w = __shfl_sync(0xffffffffu, v[k].w, src);
+          if ((lo || hi) && row_seq[rr] >= 0) {
+            // y1 = x1 cos - x2 sin (own = x1), y2 = x2 cos + x1 sin (own = x2):
+            // the operations and order of rope_rotate_pair_cs
+            const int i0 = 8 * (lo ? cc : cc - hp);
+            float cs[8], sn[8];
+            if (table) {
+              const float* tr = rtab + row_mm[rr] * 128;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                cs[j] = tr[i0 + j];
+                sn[j] = tr[64 + i0 + j];
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                sincosf(__fmul_rn(row_pos[rr], p.rope_inv_freq[i0 + j]), &sn[j], &cs[j]);
+            }
+            const uint32_t own[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+            const uint32_t oth[4] = {w.x, w.y, w.z, w.w};
+            uint32_t res[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 a = unpack2<T>(own[e]);
+              const float2 b = unpack2<T>(oth[e]);
+              float y0, y1;
+              if (lo) {
+                y0 = __fsub_rn(__fmul_rn(a.x, cs[2 * e]), __fmul_rn(b.x, sn[2 * e]));
+                y1 = __fsub_rn(__fmul_rn(a.y, cs[2 * e + 1]), __fmul_rn(b.y, sn[2 * e + 1]));
+              } else {
+                y0 = __fadd_rn(__fmul_rn(a.x, cs[2 * e]), __fmul_rn(b.x, sn[2 * e]));
+                y1 = __fadd_rn(__fmul_rn(a.y, cs[2 * e + 1]), __fmul_rn(b.y, sn[2 * e + 1]));
+              }
+              res[e] = pack2<T>(y0, y1);
+            }
+            v[k] = make_uint4(res[0], res[1], res[2], res[3]);
+          }
+        }
+        *reinterpret_cast<uint4*>(q_chunk(rr, cc)) = v[k];
       }
     }
-    if (p.rope_dim > 0) {
+    if (p.rope_dim > 0 && hp == 0) {
+      // rope_dim / 2 not a multiple of 8: element pairs in shared memory
       named_barrier(kBarConsumers, kConsumerThreads);
       for (int e = tid; e < 128 * half; e += kConsumerThreads) {
         const int rr = e / half;
         const int i = e - rr * half;
-        const int grr = row0 + rr;
-        if (grr >= rows) continue;
-        const int mm = grr / p.group;
+        if (row_seq[rr] < 0) continue;
         float cs, sn;
         if (table) {
-          cs = rtab[(mm - mem_first) * 128 + i];
-          sn = rtab[(mm - mem_first) * 128 + 64 + i];
+          cs = rtab[row_mm[rr] * 128 + i];
+          sn = rtab[row_mm[rr] * 128 + 64 + i];
         } else {
-          const int sq = p.grp_members[m0 + mm];
-          const float posf = static_cast<float>(
-              load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(sq) * p.rope_pos_stride));
-          sincosf(__fmul_rn(posf, p.rope_inv_freq[i]), &sn, &cs);
+          sincosf(__fmul_rn(row_pos[rr], p.rope_inv_freq[i]), &sn, &cs);
         }
         T* x1p = reinterpret_cast<T*>(q_chunk(rr, i >> 3) + (i & 7) * 2);
         T* x2p = reinterpret_cast<T*>(q_chunk(rr, (i + half) >> 3) + ((i + half) & 7) * 2);
@@ -2131,21 +2192,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
         }
       }
-      const int slot = p.slot0 + c;
-      if (seq >= 0) {
-        const int64_t so = seq * p.pss0 + qh * p.pss1 + slot * p.pss2;
+      if (seq_r >= 0) {
         const bool empty = !(ok && nt > 0);
-        p.pmax[so] = (empty || mrow == -INFINITY) ? -INFINITY : mrow * kLn2;  // natural-log units
-        p.psum[so] = empty ? 0.f : lrow;
+        p.pmax[so_r] = (empty || mrow == -INFINITY) ? -INFINITY : mrow * kLn2;  // natural-log units
+        p.psum[so_r] = empty ? 0.f : lrow;
       }
       named_barrier(kBarConsumers, kConsumerThreads);
       // warp w writes rows w, w + 4, ...: lane l moves 16-byte chunk l
+#pragma unroll 4
       for (int rr = warp; rr < 128; rr += kConsumerWarps) {
-        const int sq = row_seq[rr];
-        if (sq < 0) continue;  // warp-uniform (one row per iteration)
-        const int grr = row0 + rr;
-        const int hq = h * p.group + (grr - (grr / p.group) * p.group);
-        float* acc = p.pacc + sq * p.pas0 + hq * p.pas1 + slot * p.pas2;
+        if (row_seq[rr] < 0) continue;  // warp-uniform (one row per iteration)
+        float* acc = p.pacc + row_ooff[rr];
         const float4 val = *reinterpret_cast<const float4*>(ob + rr * 128 + ((lane ^ (rr & 31)) << 2));
         if (p.pas3 == 1 && (reinterpret_cast<uintptr_t>(acc) & 15u) == 0) {
           reinterpret_cast<float4*>(acc)[lane] = val;

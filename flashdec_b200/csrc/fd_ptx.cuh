@@ -175,6 +175,20 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two packed 16-bit elements (low half = lower index) as floats.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+}
+
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<__half2*>(&v));
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
 template <>

@@ -89,15 +89,29 @@ def test_cascade_matches_oracle(case):
     assert float((out.float() - plain.float()).abs().max()) <= 1.6e-2
 
 
-def test_cascade_fused_append_rope_matches_plain_fused_launch():
+# (rotary_dim, batch, hq, hkv, groups): full rotation with the per-block cos/sin
+# table; partial rotations whose half is (64 -> 32) and is not (40 -> 20) a
+# multiple of 8 elements; GQA group 2 with 40 members in one 128-row block
+# (more members than the table holds: cos/sin per element)
+ROPE_CASES = [
+    (128, 12, 16, 2, [(list(range(8)), 16), ([9, 10], 2)]),
+    (64, 12, 16, 2, [(list(range(8)), 16), ([9, 10], 2)]),
+    (40, 12, 16, 2, [(list(range(8)), 16), ([9, 10], 2)]),
+    (128, 44, 4, 2, [(list(range(40)), 6)]),
+]
+
+
+@pytest.mark.parametrize("rope_case", ROPE_CASES,
+                         ids=["rot128", "rot64", "rot40", "g2_40_members"])
+def test_cascade_fused_append_rope_matches_plain_fused_launch(rope_case):
     """Engine shape: every row appends its current token (RoPE'd K) and
     rotates q in the kernels; the cache bytes must equal those of the plain
     one-launch path and the outputs agree to the bf16 summation-order bound."""
     import flashdec_b200
     from flashdec_b200 import _native
 
-    batch, hq, hkv, d, bs, dtype = 12, 16, 2, 128, 32, "bfloat16"
-    groups = [(list(range(8)), 16), ([9, 10], 2)]
+    rot, batch, hq, hkv, groups = rope_case
+    d, bs, dtype = 128, 32, "bfloat16"
     rng, bt, lens, k, v = _build(batch, hkv, d, bs, groups, 200, dtype, seed=77)
     q = to_dev(_normal(rng, (batch, hq, d), dtype), dtype)
     ak = to_dev(_normal(rng, (batch, hkv, d), dtype), dtype)
@@ -106,8 +120,8 @@ def test_cascade_fused_append_rope_matches_plain_fused_launch():
     pos = to_dev((lens - 1).astype(np.int64))
     slot = to_dev((bt[np.arange(batch), (lens - 1) // bs].astype(np.int64) * bs
                    + (lens - 1) % bs).astype(np.int64))
-    invf = _native.inv_freq_device(128, 1e6, q.device)
-    rope = (128, invf, pos)
+    invf = _native.inv_freq_device(rot, 1e6, q.device)
+    rope = (rot, invf, pos)
     cg = _native.CascadeGroups([m for m, _ in groups], [p for _, p in groups], batch, bs,
                                q.device)
     flashdec_b200.device_status(clear=True)
@@ -128,7 +142,7 @@ def test_cascade_fused_append_rope_matches_plain_fused_launch():
     from oracle.rope import apply_rope
     from tests.test_engine_gpu import _table
 
-    q_rot = apply_rope(to_np(q), to_np(pos), 128, 1e6, dtype, _table(128, 1e6))
+    q_rot = apply_rope(to_np(q), to_np(pos), rot, 1e6, dtype, _table(rot, 1e6))
     want = paged_decode_attention_ref(q_rot, to_np(kc_b), to_np(vc_b), bt, lens)
     assert_attention_close(to_np(out_b), want)
 
