@@ -338,6 +338,7 @@ def run_ours(args, rank, world, local_rank):
         extra["c2_ctx1024"] = run_c2_ctx1024(torch, device, stream, args)
         extra["c3_rope_append"] = run_c3(torch, device, stream)
         extra["c5_engine_step"] = run_c5(torch, device, args)
+        extra["c5_layer_decode"] = run_c5_layer(torch, device, stream)
 
     if world > 1:
         dist.barrier()
@@ -649,6 +650,58 @@ def run_c5(torch, device, args, num_layers=36, num_requests=16, prefix_tokens=40
                     "layer (RoPE + K/V store + decode)"}
 
 
+def run_c5_layer(torch, device, stream, reps=300, num_requests=16, prefix_tokens=4096):
+    """One attention layer of the c5 shape through the plain decode: 16
+    requests whose block tables share the same 128 prefix pages, then private
+    tails U[1, 1025] tokens (the lengths of the engine leg's first step);
+    back-to-back paged_decode_attention_into launches, CUDA events."""
+    import numpy as np
+
+    import flashdec_b200
+    from oracle.paged_attention import attention_bytes
+
+    hq, hkv, d, bs = 16, 2, 128, 32
+    rng = np.random.default_rng(55)
+    tails = [int(x) + 1 for x in rng.integers(0, 1025, size=num_requests)]
+    pre = prefix_tokens // bs
+    rows, nxt = [], pre
+    for t in tails:
+        n = -(-t // bs)
+        rows.append(list(range(pre)) + list(range(nxt, nxt + n)))
+        nxt += n
+    width = max(len(r) for r in rows)
+    bt_h = torch.full((num_requests, width), -1, dtype=torch.int32)
+    for i, r in enumerate(rows):
+        bt_h[i, :len(r)] = torch.tensor(r, dtype=torch.int32)
+    bt = bt_h.to(device)
+    lens = [prefix_tokens + t for t in tails]
+    sl = torch.tensor(lens, dtype=torch.int32, device=device)
+    g = torch.Generator(device=device).manual_seed(7)
+    k = torch.randn((nxt, hkv, bs, d), device=device, dtype=torch.bfloat16, generator=g)
+    v = torch.randn_like(k)
+    q = torch.randn((num_requests, hq, d), device=device, dtype=torch.bfloat16, generator=g)
+    out = torch.empty_like(q)
+    with torch.cuda.stream(stream):
+        for _ in range(20):
+            flashdec_b200.paged_decode_attention_into(q, k, v, bt, sl, out)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            flashdec_b200.paged_decode_attention_into(q, k, v, bt, sl, out)
+        e1.record(stream)
+    stream.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    logical = attention_bytes(lens, hq, hkv, d, bs)
+    unique = nxt * hkv * bs * d * 2 * 2
+    return {"workload": "c5 shape, one layer, plain decode: 16 requests sharing a 4096-token "
+                        "prefix (same pages) + tails U[1,1025]",
+            "us_per_call": us, "launches": reps, "logical_kv_bytes": logical,
+            "unique_kv_bytes": unique,
+            "note": "shared prefix pages are L2 hits after the first reader: bound by the "
+                    "schedule's split-pair merges, not HBM"}
+
+
 def run_sweep(torch, device, stream):
     """Decode latency over batch x context for the Qwen attention shape
     (16q/2kv, D128, bs32, bf16), graph replay over rotating pools of at least
@@ -848,10 +901,11 @@ def main():
                     help="print decode latency over batch x context (Qwen shape), one JSON "
                          "line per point, and exit")
     ap.add_argument("--kernel-only", nargs="?", const="c2", default=None,
-                    choices=["c2", "c3", "c4"],
+                    choices=["c2", "c3", "c4", "c5"],
                     help="time only one device-resident workload (no e2e or CPU legs): c2 "
-                         "(default), c3 (fused RoPE + append) or c4 (16 requests of the ragged "
-                         "batch, 1.5 GB of KV); the small cases used for ncu captures")
+                         "(default), c3 (fused RoPE + append), c4 (16 requests of the ragged "
+                         "batch, 1.5 GB of KV) or c5 (one layer of the c5 shape, plain decode); "
+                         "the small cases used for ncu captures")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -870,7 +924,7 @@ def main():
         for point in run_sweep(torch, device, torch.cuda.Stream(device)):
             print(json.dumps({"sweep": "qwen-shape decode", **point}), flush=True)
         return
-    if args.kernel_only in ("c3", "c4"):
+    if args.kernel_only in ("c3", "c4", "c5"):
         import torch
 
         device = torch.device("cuda", 0)
@@ -878,6 +932,8 @@ def main():
         stream = torch.cuda.Stream(device)
         if args.kernel_only == "c3":
             res = run_c3(torch, device, stream, cpu_seconds=0.0, api_reps=0)
+        elif args.kernel_only == "c5":
+            res = run_c5_layer(torch, device, stream, reps=min(args.steps, 300))
         else:
             res = run_ragged(torch, None, device, 0, 1, stream, args, batch=16)
         print(json.dumps({"kernel_only": args.kernel_only, **res}), flush=True)
