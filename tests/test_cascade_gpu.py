@@ -146,3 +146,42 @@ def test_cascade_fused_append_rope_matches_plain_fused_launch(rope_case):
     want = paged_decode_attention_ref(q_rot, to_np(kc_b), to_np(vc_b), bt, lens)
     assert_attention_close(to_np(out_b), want)
 
+
+
+def test_mma_sync_prefix_pass_for_128_dim_32_token_pages():
+    """With FLASHDEC_B200_PREFIX_UMMA=0 the head_dim 128 / 32-token-page
+    cascade runs its prefix pass on mma.sync (prefix_kernel) instead of the
+    tcgen05 kernel.  The switch is read once per process, so the case runs in
+    a child process."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    code = (
+        "import sys, numpy as np, torch\n"
+        "sys.path.insert(0, %r)\n"
+        "import flashdec_b200\n"
+        "from flashdec_b200 import _native\n"
+        "from oracle import paged_decode_attention_ref\n"
+        "from tests.test_cascade_gpu import CASES, _build\n"
+        "from tests.golden.cases import _normal\n"
+        "from tests.helpers import assert_attention_close, to_dev, to_np\n"
+        "name, batch, hq, hkv, d, bs, groups, tail_max, dtype, chunks = CASES[0]\n"
+        "rng, bt, lens, k, v = _build(batch, hkv, d, bs, groups, tail_max, dtype, seed=3)\n"
+        "q = _normal(rng, (batch, hq, d), dtype)\n"
+        "want = paged_decode_attention_ref(q, k, v, bt, lens)\n"
+        "qd, kd, vd = to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype)\n"
+        "cg = _native.CascadeGroups([m for m, _ in groups], [p for _, p in groups], batch, bs,"
+        " qd.device)\n"
+        "out = torch.empty_like(qd)\n"
+        "_native.cascade_decode(qd, kd, vd, to_dev(bt), to_dev(lens), out, cg,"
+        " sm_scale=d ** -0.5, block_size=bs, num_seqs=batch)\n"
+        "torch.cuda.synchronize()\n"
+        "assert flashdec_b200.device_status(clear=True) == 0\n"
+        "assert_attention_close(to_np(out), want)\n"
+        "print('ok')\n" % str(Path(__file__).resolve().parents[1]))
+    env = dict(os.environ, FLASHDEC_B200_PREFIX_UMMA="0")
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]
