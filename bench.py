@@ -347,7 +347,9 @@ def run_ours(args, rank, world, local_rank):
     nbytes = c2_bytes()
     peak, peak_kind = _peaks()
     achieved = nbytes / (ms_per_step / 1000.0) / 1e9
-    cpu = None if args.kernel_only else cpu_baseline_sample(args)
+    # the CPU baseline is a rank-0, one-GPU figure: at N > 1 the GPUs are not
+    # held for it
+    cpu = None if (args.kernel_only or world > 1) else cpu_baseline_sample(args)
     return {
         "metric": METRIC,
         "value": world * C2["batch"] * args.steps / (max_ms / 1000.0),
