@@ -1323,6 +1323,10 @@ struct ReduceParams {
   int64_t slots;
   void* out;
   int64_t os0, os1, os2;
+  // cascade: a sequence with pre_pages[b] > 0 also merges the prefix pass's
+  // pre_slots partials in slots [num_splits, num_splits + pre_slots)
+  const int* pre_pages;
+  int pre_slots;
 };
 
 constexpr int kReduceMaxSlots = 512;
@@ -1362,7 +1366,8 @@ __global__ void split_reduce_kernel(const __grid_constant__ ReduceParams p) {
   const int64_t n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
   bool has = n > 0;
   if (p.slot) has = has && load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) >= 0;
-  const int S = min(p.num_splits, kReduceMaxSlots);
+  const int S = min(p.num_splits + ((p.pre_pages && p.pre_pages[b] > 0) ? p.pre_slots : 0),
+                    kReduceMaxSlots);
   const int64_t so = b * p.ss0 + h * p.ss1;
   float mloc = -INFINITY;
   if (has) {
@@ -2784,7 +2789,12 @@ CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c
   }
   const int64_t rows = static_cast<int64_t>(max_members) * dv.group;
   pl.row_blocks = static_cast<int>((rows + kPrefixRows - 1) / kPrefixRows);
-  pl.umma = a.head_dim == 128 && a.block_size == 32 && prefix_umma_enabled();
+  // The concurrent cascade shares the SMs between the two passes, and its
+  // prefix pass is fastest as many short mma.sync chunks (c5 layer: 24.5 us
+  // against 26.1 us for the best tcgen05 split); the serial cascade uses
+  // the tcgen05 pass.
+  const bool conc = cascade_concurrent_enabled();
+  pl.umma = a.head_dim == 128 && a.block_size == 32 && prefix_umma_enabled() && !conc;
   const int64_t units = static_cast<int64_t>(c.num_groups) * a.num_kv_heads * pl.row_blocks;
   if (c.chunks > 0) {
     pl.chunks = c.chunks;
@@ -2801,8 +2811,11 @@ CascadePlan cascade_plan(const fd_paged_decode_args& a, const fd_cascade_args& c
   if (c.tail_splits > 0) {
     pl.splits = c.tail_splits;
   } else {
-    const int64_t pairs = static_cast<int64_t>(a.num_seqs) * dv.nhb;
-    const int64_t s = (dev.num_sms + pairs - 1) / std::max<int64_t>(1, pairs);
+    const int64_t pairs = std::max<int64_t>(1, static_cast<int64_t>(a.num_seqs) * dv.nhb);
+    // serial: the tail has every SM; concurrent: the SMs the prefix CTAs leave
+    const int64_t sms = conc ? std::max<int64_t>(pairs, dev.num_sms - pl.chunks * units)
+                             : dev.num_sms;
+    const int64_t s = conc ? sms / pairs : (sms + pairs - 1) / pairs;
     pl.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, 8)));
   }
   return pl;
@@ -2815,7 +2828,7 @@ size_t cascade_scratch_bytes(const fd_paged_decode_args& a, const CascadePlan& p
 
 template <typename T, int D, int kPageRows>
 int launch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
-                  dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t stream) {
+                  dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t stream, bool pdl) {
   auto kern = prefix_kernel<T, D, kPageRows>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
@@ -2825,12 +2838,13 @@ int launch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensor
                                           dev.max_smem_optin);
   });
   if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
-  return cuda_status(launch_pdl(kern, grid, dim3(kPrefixThreads), smem, stream, prm, mk, mv));
+  return cuda_status(pdl ? launch_pdl(kern, grid, dim3(kPrefixThreads), smem, stream, prm, mk, mv)
+                         : launch_plain(kern, grid, dim3(kPrefixThreads), smem, stream, prm, mk, mv));
 }
 
 template <typename T>
 int launch_prefix_umma(const PrefixParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
-                       dim3 grid, const DeviceInfo& dev, cudaStream_t stream) {
+                       dim3 grid, const DeviceInfo& dev, cudaStream_t stream, bool pdl) {
   auto kern = prefix_umma_kernel<T>;
   const size_t smem = prefix_umma_smem_bytes();
   if (smem > static_cast<size_t>(dev.max_smem_optin)) return FD_ERR_UNSUPPORTED;
@@ -2842,19 +2856,51 @@ int launch_prefix_umma(const PrefixParams& prm, const CUtensorMap& mk, const CUt
                                           static_cast<int>(smem));
   });
   if (attr_err[slot] != cudaSuccess) return cuda_status(attr_err[slot]);
-  return cuda_status(launch_pdl(kern, grid, dim3(kThreads), smem, stream, prm, mk, mv));
+  return cuda_status(pdl ? launch_pdl(kern, grid, dim3(kThreads), smem, stream, prm, mk, mv)
+                         : launch_plain(kern, grid, dim3(kThreads), smem, stream, prm, mk, mv));
 }
 
 template <typename T, int D>
 int dispatch_prefix(const PrefixParams& prm, const CUtensorMap& mk, const CUtensorMap& mv,
-                    dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st) {
+                    dim3 grid, size_t smem, const DeviceInfo& dev, cudaStream_t st, bool pdl) {
   if constexpr (D == 128) {
     if (prm.kperm[3] >= 0) {
-      return prm.block_size == 16 ? launch_prefix<T, D, 16>(prm, mk, mv, grid, smem, dev, st)
-                                  : launch_prefix<T, D, 8>(prm, mk, mv, grid, smem, dev, st);
+      return prm.block_size == 16
+                 ? launch_prefix<T, D, 16>(prm, mk, mv, grid, smem, dev, st, pdl)
+                 : launch_prefix<T, D, 8>(prm, mk, mv, grid, smem, dev, st, pdl);
     }
   }
-  return launch_prefix<T, D, 0>(prm, mk, mv, grid, smem, dev, st);
+  return launch_prefix<T, D, 0>(prm, mk, mv, grid, smem, dev, st, pdl);
+}
+
+// Per-device second stream and fork / join events of the concurrent cascade
+// (created on the first such call on the device, with that device current;
+// a mutex keeps calls from different host threads from interleaving their
+// fork and join).
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex mu;
+  cudaError_t err = cudaSuccess;
+};
+SideStream g_side[64];
+std::once_flag g_side_once[64];
+
+SideStream* side_stream(int device) {
+  SideStream& ss = g_side[device & 63];
+  std::call_once(g_side_once[device & 63], [&] {
+    ss.err = cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking);
+    if (ss.err == cudaSuccess) ss.err = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming);
+    if (ss.err == cudaSuccess) ss.err = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming);
+  });
+  return ss.err == cudaSuccess ? &ss : nullptr;
+}
+
+template <typename T>
+int launch_reduce(const ReduceParams& p, int head_dim, cudaStream_t stream) {
+  const dim3 grid(p.num_seqs, p.num_q_heads);
+  const int threads = head_dim >= 128 ? 128 : 64;
+  return cuda_status(launch_plain(split_reduce_kernel<T>, grid, dim3(threads), 0, stream, p));
 }
 
 }  // namespace
@@ -2962,23 +3008,22 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   const dim3 pgrid(static_cast<unsigned>(pl.chunks), static_cast<unsigned>(pl.row_blocks),
                    static_cast<unsigned>(c->num_groups * a->num_kv_heads));
   const bool bf16 = a->dtype == FD_DTYPE_BF16;
-  if (pl.umma && pp.kperm[3] < 0) {
-    rc = bf16 ? launch_prefix_umma<__nv_bfloat16>(pp, mk, mv, pgrid, *dev, stream)
-              : launch_prefix_umma<__half>(pp, mk, mv, pgrid, *dev, stream);
-  } else if (D == 128) {
-    rc = bf16 ? dispatch_prefix<__nv_bfloat16, 128>(pp, mk, mv, pgrid, psmem, *dev, stream)
-              : dispatch_prefix<__half, 128>(pp, mk, mv, pgrid, psmem, *dev, stream);
-  } else {
-    rc = bf16 ? dispatch_prefix<__nv_bfloat16, 64>(pp, mk, mv, pgrid, psmem, *dev, stream)
-              : dispatch_prefix<__half, 64>(pp, mk, mv, pgrid, psmem, *dev, stream);
-  }
-  if (rc) return rc;
+  auto launch_prefix_pass = [&](cudaStream_t st, bool pdl) {
+    if (pl.umma && pp.kperm[3] < 0) {
+      return bf16 ? launch_prefix_umma<__nv_bfloat16>(pp, mk, mv, pgrid, *dev, st, pdl)
+                  : launch_prefix_umma<__half>(pp, mk, mv, pgrid, *dev, st, pdl);
+    }
+    if (D == 128) {
+      return bf16 ? dispatch_prefix<__nv_bfloat16, 128>(pp, mk, mv, pgrid, psmem, *dev, st, pdl)
+                  : dispatch_prefix<__half, 128>(pp, mk, mv, pgrid, psmem, *dev, st, pdl);
+    }
+    return bf16 ? dispatch_prefix<__nv_bfloat16, 64>(pp, mk, mv, pgrid, psmem, *dev, st, pdl)
+                : dispatch_prefix<__half, 64>(pp, mk, mv, pgrid, psmem, *dev, st, pdl);
+  };
 
-  // ---- tail pass: split decode after the shared pages; the pair's last
-  // CTA merges the tail splits and (members) the prefix chunks ----
+  // tail pass: split decode after the shared pages, partials in slots [0, S)
   fd_paged_decode_args t = *a;
   t.num_splits = pl.splits;
-  t.epilogue = FD_EPILOGUE_FUSED;
   t.part_acc = acc;
   t.part_acc_stride[0] = pp.pas0;
   t.part_acc_stride[1] = pp.pas1;
@@ -2989,5 +3034,65 @@ extern "C" int fd_cascade_decode(const fd_paged_decode_args* a, const fd_cascade
   t.part_stat_stride[0] = pp.pss0;
   t.part_stat_stride[1] = pp.pss1;
   t.part_stat_stride[2] = 1;
-  return paged_decode_impl(&t, c->seq_prefix_pages, pl.chunks, cuda_stream);
+
+  if (!cascade_concurrent_enabled()) {
+    // prefix pass, then the tail, whose pair-last CTA merges the S tail
+    // splits and (members) the C prefix chunks through the tickets
+    rc = launch_prefix_pass(stream, true);
+    if (rc) return rc;
+    t.epilogue = FD_EPILOGUE_FUSED;
+    return paged_decode_impl(&t, c->seq_prefix_pages, pl.chunks, cuda_stream);
+  }
+
+  // Concurrent: the prefix pass runs on a second stream beside the tail pass
+  // (neither reads what the other writes; together they fit the SMs of a
+  // small batch), then one reduction merges S tail + C prefix partials per
+  // member row and the S tail partials of the other rows.
+  SideStream* ss = side_stream(dev->device);
+  if (!ss) return FD_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(ss->mu);
+  cudaError_t e = cudaEventRecord(ss->fork, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->stream, ss->fork, 0);
+  if (e != cudaSuccess) return cuda_status(e);
+  int prc = launch_prefix_pass(ss->stream, false);
+  // the join is recorded and waited on whatever happened, so the caller's
+  // stream (or its capture) never leaves the second stream behind
+  e = cudaEventRecord(ss->join, ss->stream);
+  t.epilogue = FD_EPILOGUE_PARTIALS;
+  int trc = paged_decode_impl(&t, c->seq_prefix_pages, 0, cuda_stream);
+  const cudaError_t e2 = cudaStreamWaitEvent(stream, ss->join, 0);
+  if (prc) return prc;
+  if (trc) return trc;
+  if (e != cudaSuccess) return cuda_status(e);
+  if (e2 != cudaSuccess) return cuda_status(e2);
+
+  ReduceParams rp;
+  std::memset(&rp, 0, sizeof(rp));
+  rp.num_seqs = a->num_seqs;
+  rp.num_q_heads = a->num_q_heads;
+  rp.head_dim = D;
+  rp.num_splits = pl.splits;
+  rp.pre_pages = c->seq_prefix_pages;
+  rp.pre_slots = pl.chunks;
+  rp.acc = acc;
+  rp.as0 = pp.pas0;
+  rp.as1 = pp.pas1;
+  rp.as2 = pp.pas2;
+  rp.as3 = 1;
+  rp.mx = mx;
+  rp.sm = sm;
+  rp.ss0 = pp.pss0;
+  rp.ss1 = pp.pss1;
+  rp.ss2 = 1;
+  rp.sl = a->seq_lens;
+  rp.sl64 = a->seq_lens_index == FD_INDEX_I64;
+  rp.sls = a->seq_lens_stride;
+  rp.slot = a->slot_mapping;
+  rp.slot64 = a->slot_mapping_index == FD_INDEX_I64;
+  rp.slots = a->slot_mapping_stride;
+  rp.out = a->out;
+  rp.os0 = a->out_stride[0];
+  rp.os1 = a->out_stride[1];
+  rp.os2 = a->out_stride[2];
+  return bf16 ? launch_reduce<__nv_bfloat16>(rp, D, stream) : launch_reduce<__half>(rp, D, stream);
 }

@@ -113,6 +113,14 @@ bool pdl_enabled() {
   return on;
 }
 
+bool cascade_concurrent_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLASHDEC_B200_CASCADE_CONCURRENT");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 bool cluster_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("FLASHDEC_B200_CLUSTER");

@@ -82,4 +82,25 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// The same launch without the attribute, for a kernel whose stream
+// predecessor is an event wait (a fork or join between streams) instead of
+// a kernel it could overlap.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_plain(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// Whether fd_cascade_decode runs the prefix pass on a second stream beside
+// the tail pass (default on; FLASHDEC_B200_CASCADE_CONCURRENT=0 runs prefix
+// then tail on the caller's stream, the tail merging through tickets).
+bool cascade_concurrent_enabled();
+
 }  // namespace fd

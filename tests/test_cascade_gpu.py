@@ -148,11 +148,17 @@ def test_cascade_fused_append_rope_matches_plain_fused_launch(rope_case):
 
 
 
-def test_mma_sync_prefix_pass_for_128_dim_32_token_pages():
-    """With FLASHDEC_B200_PREFIX_UMMA=0 the head_dim 128 / 32-token-page
-    cascade runs its prefix pass on mma.sync (prefix_kernel) instead of the
-    tcgen05 kernel.  The switch is read once per process, so the case runs in
-    a child process."""
+@pytest.mark.parametrize("env", [{"FLASHDEC_B200_CASCADE_CONCURRENT": "0"},
+                                 {"FLASHDEC_B200_CASCADE_CONCURRENT": "0",
+                                  "FLASHDEC_B200_PREFIX_UMMA": "0"}],
+                         ids=["serial_tcgen05_prefix", "serial_mma_sync_prefix"])
+def test_serial_cascade_paths(env):
+    """The default cascade runs the prefix and tail passes concurrently and
+    merges in one reduction (the other tests here).  With
+    FLASHDEC_B200_CASCADE_CONCURRENT=0 the passes run one after the other and
+    the tail merges through tickets; head_dim 128 / 32-token pages then take
+    the tcgen05 prefix pass unless FLASHDEC_B200_PREFIX_UMMA=0.  The switches
+    are read once per process, so the cases run in a child process."""
     import os
     import subprocess
     import sys
@@ -167,21 +173,21 @@ def test_mma_sync_prefix_pass_for_128_dim_32_token_pages():
         "from tests.test_cascade_gpu import CASES, _build\n"
         "from tests.golden.cases import _normal\n"
         "from tests.helpers import assert_attention_close, to_dev, to_np\n"
-        "name, batch, hq, hkv, d, bs, groups, tail_max, dtype, chunks = CASES[0]\n"
-        "rng, bt, lens, k, v = _build(batch, hkv, d, bs, groups, tail_max, dtype, seed=3)\n"
-        "q = _normal(rng, (batch, hq, d), dtype)\n"
-        "want = paged_decode_attention_ref(q, k, v, bt, lens)\n"
-        "qd, kd, vd = to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype)\n"
-        "cg = _native.CascadeGroups([m for m, _ in groups], [p for _, p in groups], batch, bs,"
-        " qd.device)\n"
-        "out = torch.empty_like(qd)\n"
-        "_native.cascade_decode(qd, kd, vd, to_dev(bt), to_dev(lens), out, cg,"
+        "for case in CASES[:2]:\n"
+        "    name, batch, hq, hkv, d, bs, groups, tail_max, dtype, chunks = case\n"
+        "    rng, bt, lens, k, v = _build(batch, hkv, d, bs, groups, tail_max, dtype, seed=3)\n"
+        "    q = _normal(rng, (batch, hq, d), dtype)\n"
+        "    want = paged_decode_attention_ref(q, k, v, bt, lens)\n"
+        "    qd, kd, vd = to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype)\n"
+        "    cg = _native.CascadeGroups([m for m, _ in groups], [p for _, p in groups], batch,"
+        " bs, qd.device)\n"
+        "    out = torch.empty_like(qd)\n"
+        "    _native.cascade_decode(qd, kd, vd, to_dev(bt), to_dev(lens), out, cg,"
         " sm_scale=d ** -0.5, block_size=bs, num_seqs=batch)\n"
-        "torch.cuda.synchronize()\n"
-        "assert flashdec_b200.device_status(clear=True) == 0\n"
-        "assert_attention_close(to_np(out), want)\n"
+        "    torch.cuda.synchronize()\n"
+        "    assert flashdec_b200.device_status(clear=True) == 0\n"
+        "    assert_attention_close(to_np(out), want)\n"
         "print('ok')\n" % str(Path(__file__).resolve().parents[1]))
-    env = dict(os.environ, FLASHDEC_B200_PREFIX_UMMA="0")
-    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
-                         timeout=300)
+    res = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, **env),
+                         capture_output=True, text=True, timeout=300)
     assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]
