@@ -159,10 +159,17 @@ int fd_paged_decode(const fd_paged_decode_args* args, void* cuda_stream);
  * registered once and attached to every member: flashdec/cache.py:192-276).
  * The shared pages are read once per KV head for all of a group's query rows
  * (prefix pass, 128 rows per CTA, one partial per chunk of pages); the rest of
- * every sequence goes through the split decode (tail pass), whose last CTA
- * per (sequence, head block) merges the split partials and the member's
- * prefix partials (LSE merge of flashdec/kernels/paged_decode.py:593-635).
- * Two launches on the stream.  args->num_splits, epilogue and part_* are
+ * every sequence goes through the split decode (tail pass).  By default the
+ * prefix pass runs on a second stream of the library's own beside the tail
+ * pass on the caller's stream (fork and join by events: capturable), and one
+ * reduction then merges each row's tail and prefix partials (LSE merge of
+ * flashdec/kernels/paged_decode.py:593-635): three launches.  The second
+ * stream and its two events are created by the first such call on a device
+ * (that device current; make it before any stream capture); calls from
+ * several host threads take turns on them.  With
+ * FLASHDEC_B200_CASCADE_CONCURRENT=0 the two passes run one after the other
+ * on the caller's stream and the tail's last CTA per (sequence, head block)
+ * merges through the tickets: two launches.  args->num_splits, epilogue and part_* are
  * ignored; args->scratch and args->tickets must hold fd_cascade_workspace's
  * sizes (tickets zero-filled once; the kernels leave them zero).  The group
  * description lives in HOST memory and is copied into the launch; every
