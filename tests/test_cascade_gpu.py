@@ -191,3 +191,35 @@ def test_serial_cascade_paths(env):
     res = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, **env),
                          capture_output=True, text=True, timeout=300)
     assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]
+
+
+def test_concurrent_cascade_replays_from_a_cuda_graph():
+    """The concurrent cascade forks a second stream and joins it back with
+    events, so it can be captured: a graph of the call replays to the eager
+    call's output, bit for bit (same kernels, same partial order)."""
+    import flashdec_b200
+    from flashdec_b200 import _native
+
+    name, batch, hq, hkv, d, bs, groups, tail_max, dtype, chunks = CASES[0]
+    rng, bt, lens, k, v = _build(batch, hkv, d, bs, groups, tail_max, dtype, seed=11)
+    q = _normal(rng, (batch, hq, d), dtype)
+    qd, kd, vd = to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype)
+    btd, sld = to_dev(bt), to_dev(lens)
+    cg = _native.CascadeGroups([m for m, _ in groups], [p for _, p in groups], batch, bs,
+                               qd.device)
+    eager = torch.empty_like(qd)
+    kw = dict(sm_scale=d ** -0.5, block_size=bs, num_seqs=batch)
+    _native.cascade_decode(qd, kd, vd, btd, sld, eager, cg, **kw)  # also sets up the streams
+    torch.cuda.synchronize()
+    out = torch.full_like(qd, float("nan"))
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        _native.cascade_decode(qd, kd, vd, btd, sld, out, cg, **kw)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert flashdec_b200.device_status(clear=True) == 0
+    assert torch.equal(out, eager)
+    del graph
