@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 INCLUDE = REPO / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libflashdec_b200.so"
-SOURCES = ["fd_host.cu", "fd_attention.cu", "fd_rope_append.cu", "fd_static.cu", "fd_selftest.cu"]
+SOURCES = ["fd_host.cu", "fd_attention.cu", "fd_wave_decode.cu", "fd_rope_append.cu", "fd_static.cu", "fd_selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
          "-I", str(INCLUDE), "-I", str(CSRC)]

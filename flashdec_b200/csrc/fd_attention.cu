@@ -49,10 +49,11 @@
 
 #include "fd_host.h"
 #include "fd_ptx.cuh"
+#include "fd_tile.cuh"
+#include "fd_wave_decode.h"
 
 namespace fd {
 
-constexpr int kTile = 32;  // tokens per tile
 constexpr int kConsumerWarps = 4;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
@@ -144,59 +145,6 @@ struct Smem {
   static constexpr int kMergeBytes = kMergeFloats * 4 + kConsumerWarps * kMaxRows * 8;
 };
 
-// Column of element (row, col) in a merge buffer of 128-float-aligned rows:
-// XOR with 8 * (row % 4) so that consecutive rows start on different banks.
-__device__ __forceinline__ int merge_col(int row, int col) { return col ^ ((row & 3) << 3); }
-
-// Stage tiles (one 32-token tile of K or V).  Default layout (kPageRows 0):
-// D/64 halves of [32 rows][64 dims], one TMA box per (page, half).  With
-// kPageRows = 16 or 8 (head_dim 128, pages of that many tokens, one box per
-// page plane): [page][half][kPageRows rows][64 dims].  Both carry the TMA
-// 128B swizzle, which depends only on the shared-memory address (16-byte
-// chunk index XOR address bits 7-9 = row % 8; every half of a page starts on
-// a 1 KB boundary).
-template <int kPageRows>
-__device__ __forceinline__ uint32_t stage_row_base(int row, int half) {
-  if constexpr (kPageRows > 0) {
-    return (row / kPageRows) * (kPageRows * 256) + half * (kPageRows * 128) +
-           (row % kPageRows) * 128;
-  } else {
-    return half * (kTile * 128) + row * 128;
-  }
-}
-// Byte distance of 16 tile rows and of one 64-dim half in a stage, for the
-// per-lane ldmatrix offsets that are hoisted out of the tile loop: row
-// r + 16 np of half h of chunk (8 h + c8) sits at
-//   stage_row_base(r, 0) + np * kRows16Bytes + h * kHalfStride + ((c8 ^ (r % 8)) << 4)
-// for r < 16 (a multiple-of-8 row shift keeps r % 8, hence the swizzle).
-template <int kPageRows>
-struct StageStrides {
-  static constexpr uint32_t kRows16Bytes = kPageRows > 0 ? (16 / kPageRows) * (kPageRows * 256) : 16 * 128;
-  static constexpr uint32_t kHalfStride = kPageRows > 0 ? kPageRows * 128 : kTile * 128;
-};
-
-template <int kPageRows>
-__device__ __forceinline__ uint32_t stage_tile_offset(int row, int dim) {
-  const int dd = dim & 63;
-  return stage_row_base<kPageRows>(row, dim >> 6) + (((dd >> 3) ^ (row & 7)) << 4) +
-         ((dd & 7) << 1);
-}
-template <int kPageRows>
-__device__ __forceinline__ uint32_t stage_chunk_offset(int row, int chunk) {
-  return stage_row_base<kPageRows>(row, chunk >> 3) + (((chunk & 7) ^ (row & 7)) << 4);
-}
-
-// Byte offset of element (row, dim) in a [32][D] tile stored as D/64 halves
-// of [32][64] with the TMA 128B swizzle (16-byte chunk index XOR row % 8).
-__device__ __forceinline__ uint32_t tile_offset(int row, int dim) {
-  const int dd = dim & 63;
-  return (dim >> 6) * (kTile * 128) + row * 128 + (((dd >> 3) ^ (row & 7)) << 4) + ((dd & 7) << 1);
-}
-
-// Byte offset of 16-byte chunk `chunk` (8 dims) of `row`.
-__device__ __forceinline__ uint32_t chunk_offset(int row, int chunk) {
-  return (chunk >> 3) * (kTile * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
-}
 
 struct SeqInfo {
   int n;      // tokens attended (0 => nothing to attend: zero output)
@@ -409,9 +357,6 @@ __device__ __forceinline__ void store_out4(const AttnParams& p, int b, int h, in
   o[3 * p.os2] = from_f32<T>(a3);
 }
 
-__device__ __forceinline__ int tmap_coord(int axis, int kv_head, int blk) {
-  return axis == 1 ? kv_head : (axis == 2 ? blk : 0);  // token and half start at 0
-}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -2677,6 +2622,85 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
                                 : smem_bytes<64>(stages, sched_ints, fa);
 
   const bool bf16 = a->dtype == FD_DTYPE_BF16;
+  // Small batches (the balanced split plan) run as one wave of CTAs that fit
+  // two per SM, so the next call's CTAs overlap this one (fd_wave_decode.cu).
+  if (tma && plan.balanced && !p.fused_append && !pre_pages &&
+      a->epilogue == FD_EPILOGUE_FUSED && wave_enabled()) {
+    WaveParams w;
+    std::memset(&w, 0, sizeof(w));
+    w.num_seqs = p.num_seqs;
+    w.num_blocks = p.num_blocks;
+    w.max_blocks = p.max_blocks;
+    w.block_size = p.block_size;
+    w.group = p.group;
+    w.hb_per_kv = p.hb_per_kv;
+    w.rows = p.rows;
+    w.cap_tiles = p.cap_tiles;
+    w.scale_log2 = p.scale_log2;
+    w.q = p.q;
+    w.qs0 = p.qs0;
+    w.qs1 = p.qs1;
+    w.qs2 = p.qs2;
+    w.out = p.out;
+    w.os0 = p.os0;
+    w.os1 = p.os1;
+    w.os2 = p.os2;
+    std::copy(p.kperm, p.kperm + 4, w.kperm);
+    std::copy(p.vperm, p.vperm + 4, w.vperm);
+    w.k = p.k;
+    w.ks0 = p.ks0;
+    w.ks1 = p.ks1;
+    w.ks2 = p.ks2;
+    w.v = p.v;
+    w.vs0 = p.vs0;
+    w.vs1 = p.vs1;
+    w.vs2 = p.vs2;
+    w.bt = p.bt;
+    w.bt64 = p.bt64;
+    w.bts0 = p.bts0;
+    w.bts1 = p.bts1;
+    w.sl = p.sl;
+    w.sl64 = p.sl64;
+    w.sls = p.sls;
+    w.pacc = p.pacc;
+    w.pas0 = p.pas0;
+    w.pas1 = p.pas1;
+    w.pas2 = p.pas2;
+    w.pas3 = p.pas3;
+    w.pmax = p.pmax;
+    w.psum = p.psum;
+    w.pss0 = p.pss0;
+    w.pss1 = p.pss1;
+    w.pss2 = p.pss2;
+    w.tickets = p.tickets;
+    w.status = p.status;
+    // head_dim 128: maps whose box is a whole page plane (the 32-token
+    // maps above move one 64-dim half per box)
+    CUtensorMap wk = mk, wv = mv;
+    bool wtma = true;
+    if (D == 128 && a->block_size == 32) {
+      for (int plane = 0; plane < 2 && wtma; ++plane) {
+        CacheDesc cd;
+        cd.base = plane ? a->v_cache : a->k_cache;
+        cd.elem_bytes = 2;
+        cd.is_bf16 = a->dtype == FD_DTYPE_BF16;
+        cd.head_dim = D;
+        cd.block_size = a->block_size;
+        cd.num_heads = a->num_kv_heads;
+        cd.num_blocks = a->num_blocks;
+        const int64_t* st = plane ? a->v_stride : a->k_stride;
+        for (int i = 0; i < 4; ++i) cd.stride[i] = st[i];
+        if (cd.num_heads == 1) cd.stride[1] = cd.stride[0];
+        cd.plane_box = 1;
+        wtma = get_cache_tensor_map(cd, plane ? &wv : &wk, plane ? w.vperm : w.kperm);
+      }
+    }
+    if (wtma) {
+      const int page_rows = (D == 128 && a->block_size < 32) ? a->block_size : 0;
+      const int wrc = wave_decode(w, wk, wv, bf16, D, page_rows, gdim, *dev, stream);
+      if (wrc != FD_ERR_UNSUPPORTED) return wrc;
+    }
+  }
   if (D == 128) {
     return bf16 ? dispatch<__nv_bfloat16, 128>(tma, p, mk, mv, gdim, smem, *dev, stream)
                 : dispatch<__half, 128>(tma, p, mk, mv, gdim, smem, *dev, stream);

@@ -48,9 +48,10 @@ struct MapKey {
   const void* base;
   int elem_bytes, is_bf16, head_dim, block_size, num_heads, num_blocks;
   int64_t stride[4];
+  int plane_box;
   bool operator==(const MapKey& o) const {
     return base == o.base && elem_bytes == o.elem_bytes && is_bf16 == o.is_bf16 &&
-           head_dim == o.head_dim &&
+           head_dim == o.head_dim && plane_box == o.plane_box &&
            block_size == o.block_size && num_heads == o.num_heads &&
            num_blocks == o.num_blocks && std::memcmp(stride, o.stride, sizeof(stride)) == 0;
   }
@@ -152,7 +153,7 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
     if (bytes <= 0 || bytes % 16 != 0 || bytes >= (int64_t(1) << 40)) return false;
   }
   MapKey key{d.base, d.elem_bytes, d.is_bf16, d.head_dim, d.block_size, d.num_heads, d.num_blocks,
-             {d.stride[0], d.stride[1], d.stride[2], d.stride[3]}};
+             {d.stride[0], d.stride[1], d.stride[2], d.stride[3]}, d.plane_box};
   {
     std::lock_guard<std::mutex> lock(g_map_mu);
     for (auto& e : g_maps) {
@@ -186,7 +187,8 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
   }};
   std::stable_sort(ax.begin(), ax.end(),
                    [](const Axis& a, const Axis& b) { return a.stride_bytes < b.stride_bytes; });
-  const bool halves = d.head_dim == 128 && (d.block_size == 16 || d.block_size == 8);
+  const bool halves =
+      d.head_dim == 128 && (d.block_size == 16 || d.block_size == 8 || d.plane_box != 0);
   std::array<Axis, 4> all;
   int n = 0;
   for (const Axis& a : ax) {

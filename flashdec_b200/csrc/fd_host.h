@@ -32,12 +32,15 @@ struct CacheDesc {
   int num_heads;
   int num_blocks;
   int64_t stride[4];    // block, head, token, dim (elements)
+  int plane_box = 0;    // head_dim 128: the half axis for every page size, so one
+                        // box moves a whole page plane (also 32-token pages)
 };
 
 // Encode (or fetch from the cache) a tiled tensor map over `d` with 128B
 // swizzle whose box is one page plane: [64 dims x block_size tokens x 1 head
-// x 1 block] (4-D), or, for head_dim 128 with 16- or 8-token pages, the same
-// plus a "64-dim half" axis of box 2 (5-D) so one copy moves the whole plane.
+// x 1 block] (4-D), or, for head_dim 128 with 16- or 8-token pages (any page
+// size with `plane_box`), the same plus a "64-dim half" axis of box 2 (5-D) so
+// one copy moves the whole plane.
 // `perm[i]` receives which axis tensor-map dimension i+1 is (0 token, 1 head,
 // 2 block, 3 half; -1 unused); outer axes are sorted by ascending stride and
 // the half axis follows the token axis.  Returns false when the layout cannot

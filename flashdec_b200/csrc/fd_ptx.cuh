@@ -111,6 +111,47 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Tiled TMA prefetch of one box into L2 (no shared memory, no barrier).  A
+// prefetch is a hint: it moves no data into this CTA and cannot return stale
+// values, because L2 is where every SM's writes become visible.
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                int c3) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_5d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+// Prefetch the 128-byte line holding `p` into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
+}
+
+// One integer element (int32 or int64 storage) loaded through L2 only
+// (ld.global.cg: nothing is left in L1 for a later load to hit).
+__device__ __forceinline__ int64_t load_index_cg(const void* base, int is64, int64_t i) {
+  return is64 ? static_cast<int64_t>(__ldcg(static_cast<const long long*>(base) + i))
+              : static_cast<int64_t>(__ldcg(static_cast<const int*>(base) + i));
+}
+
+// Transpose of an 8x8 matrix of 16-bit elements held in the mma fragment
+// layout (lane l holds row l / 4, columns 2 (l % 4) and 2 (l % 4) + 1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -356,6 +397,11 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release;" ::: "memory");
 }
+// Arrive without release semantics (nothing this thread wrote needs to be
+// published through the barrier itself).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
 }
@@ -376,6 +422,25 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
 __device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b)
                : "memory");
+}
+
+// Asynchronous store into shared memory of a CTA of the cluster (possibly
+// this one); completion is counted in bytes on `bar_cluster`, an mbarrier of
+// the same CTA as the destination, so the receiver learns from its own
+// barrier phase that the data has landed.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float a, float b, float c, float d,
+                                            uint32_t bar_cluster) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          addr),
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uint32_t bar_cluster) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+      "f"(a), "f"(b), "r"(bar_cluster)
+      : "memory");
 }
 
 // Arrive on an mbarrier of another CTA of the cluster, releasing at cluster
