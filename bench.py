@@ -42,6 +42,7 @@ METRIC = ("paged decode attn p50 µs & HBM GB/s (% of peak), B8 ctx2048; "
           "tok/s at 1–8 GPUs")
 C2 = dict(batch=8, hq=16, hkv=2, d=128, bs=32, ctx=2048, pool_factor=2)
 NUM_POOLS = 12
+E2E_STEPS = 2400  # end-to-end steps timed (a multiple of NUM_POOLS and of the two streams)
 
 
 def _peaks():
@@ -170,6 +171,18 @@ def run_ours(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    # clocks are sampled over the whole run (warm-up, timed region and every
+    # leg), so the record always has samples
+    clocks = ClockSampler(torch.cuda.current_device()).__enter__()
+    try:
+        return _run_ours(args, rank, world, torch, dist, device, clocks)
+    finally:
+        clocks.__exit__(None, None, None)
+
+
+def _run_ours(args, rank, world, torch, dist, device, clocks):
+    import flashdec_b200
+
     pools, sl = build_c2_pools(torch, device, seed=1234 + rank)
     outs = [torch.empty_like(p["q"]) for p in pools]
     stream = torch.cuda.Stream(device)
@@ -209,15 +222,17 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            if graph_rem is not None:
-                graph_rem.replay()
-            end.record(stream)
-        stream.synchronize()
+    with torch.cuda.stream(stream):
+        # the GPU is kept busy while the host enqueues the replays, so the
+        # events time device work only
+        torch.cuda._sleep(200000)
+        start.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        if graph_rem is not None:
+            graph_rem.replay()
+        end.record(stream)
+    stream.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -256,10 +271,13 @@ def run_ours(args, rank, world, local_rank):
     # writes a preallocated output, which is read back by one D2H copy.
     # Consecutive steps alternate between two streams with their own device
     # buffers (double buffering), so one step's copies overlap the other's
-    # kernel; a step's three operations stay in order on its stream.
+    # kernel; a step's three operations stay in order on its stream, and each
+    # stream has its own decode workspace.  The step count does not depend on
+    # --steps (E2E_STEPS), so start-up does not dominate; every step's output
+    # lands in its own pinned buffer and all of them are checked afterwards.
     e2e = None
     if not args.kernel_only:
-        e2e_steps = min(args.steps, 3000)
+        e2e_steps = E2E_STEPS
 
         def seg(nbytes):
             return (nbytes + 255) // 256 * 256
@@ -289,9 +307,8 @@ def run_ours(args, rank, world, local_rank):
         darenas = [torch.empty(arena_nb, dtype=torch.uint8, device=device) for _ in range(nbuf)]
         dviews = [views(x) for x in darenas]
         douts = [torch.empty_like(pools[0]["q"]) for _ in range(nbuf)]
-        # hout[j] is rewritten every NUM_POOLS (even) steps, on the same stream
-        hout = [torch.empty_like(p["q"], device="cpu").pin_memory() for p in pools]
-        dout = douts[0]
+        hout = torch.empty((e2e_steps,) + tuple(pools[0]["q"].shape),
+                           dtype=pools[0]["q"].dtype).pin_memory()
 
         def e2e_step(i):
             j = i % NUM_POOLS
@@ -301,10 +318,10 @@ def run_ours(args, rank, world, local_rank):
             darenas[bb].copy_(harena[j], non_blocking=True)
             flashdec_b200.paged_decode_attention_into(dq, pools[j]["k"], pools[j]["v"], dbt, dsl,
                                                       douts[bb])
-            hout[j].copy_(douts[bb], non_blocking=True)
+            hout[i].copy_(douts[bb], non_blocking=True)
 
         with torch.cuda.stream(stream):
-            for i in range(20):
+            for i in range(2 * NUM_POOLS):
                 e2e_step(i)
         torch.cuda.synchronize()
         if world > 1:
@@ -312,22 +329,20 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         with torch.cuda.stream(stream):
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
             for i in range(e2e_steps):
                 e2e_step(i)
-            s1.record(stream)
         torch.cuda.synchronize()  # both step streams
         wall = time.perf_counter() - t0
-        ev_ms = s0.elapsed_time(s1)
-        # the last step's host output equals a device-resident decode of its inputs
-        jl = (e2e_steps - 1) % NUM_POOLS
-        chk = flashdec_b200.decode(pools[jl]["q"], pools[jl]["k"], pools[jl]["v"], pools[jl]["bt"],
-                                   sl)
-        if not torch.equal(hout[jl], chk.cpu()):
-            raise RuntimeError("e2e output differs from the device-resident decode of its inputs")
-        te = torch.tensor([max(ev_ms, wall * 1000.0)], device=device, dtype=torch.float64)
+        # every step's host output equals a device-resident decode of its pool
+        expect = torch.stack([flashdec_b200.decode(pools[j]["q"], pools[j]["k"], pools[j]["v"],
+                                                   pools[j]["bt"], sl).cpu()
+                              for j in range(NUM_POOLS)])
+        idx = torch.arange(e2e_steps) % NUM_POOLS
+        if not torch.equal(hout, expect[idx]):
+            bad = int((hout != expect[idx]).flatten(1).any(1).sum())
+            raise RuntimeError(f"e2e: {bad} of {e2e_steps} steps differ from the device-resident "
+                               "decode of their inputs")
+        te = torch.tensor([wall * 1000.0], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = float(te.item())
@@ -335,11 +350,13 @@ def run_ours(args, rank, world, local_rank):
             "value": world * C2["batch"] * e2e_steps / (e2e_ms / 1000.0),
             "unit": "tokens/s",
             "h2d_bytes_per_step": int(arena_nb),
-            "d2h_bytes_per_step": int(dout.numel() * dout.element_size()),
+            "d2h_bytes_per_step": int(douts[0].numel() * douts[0].element_size()),
             "steps": e2e_steps,
+            "us_per_step": e2e_ms * 1000.0 / e2e_steps,
             "api": "flashdec_b200.paged_decode_attention_into; q, block tables and seq_lens in one "
                    "pinned host arena, one H2D and one D2H copy per step; steps alternate "
-                   "between two streams with their own device buffers",
+                   "between two streams with their own device buffers and workspaces",
+            "check": f"all {e2e_steps} host outputs equal the device-resident decode of their inputs",
             "timing": "wall clock between device-wide synchronisations",
         }
 
@@ -351,6 +368,13 @@ def run_ours(args, rank, world, local_rank):
         extra["c3_rope_append"] = run_c3(torch, device, stream)
         extra["c5_engine_step"] = run_c5(torch, device, args)
         extra["c5_layer_decode"] = run_c5_layer(torch, device, stream)
+        # BASELINE config 1 is a CPU config (fp32, which the GPU path does not
+        # take): the reference CPU path timed on it beside c2
+        c1 = cpu_baseline_sample(args, seconds=float(os.environ.get("FD_C1_SECONDS", "3")),
+                                 workload="c1")
+        c1["workload"] = ("BASELINE c1: B4, 16q/2kv, D128, bs32, fp32, seq U[64,512], 128-block "
+                          "permuted pool (CPU only)")
+        extra["c1_cpu"] = c1
 
     if world > 1:
         dist.barrier()
@@ -378,15 +402,9 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, scattered block tables)",
-        "config": {
-            "workload": "BASELINE c2: Qwen2.5-3B-shape paged decode attention, B8 ctx2048",
-            "batch_per_gpu": C2["batch"], "q_heads": C2["hq"], "kv_heads": C2["hkv"],
-            "head_dim": C2["d"], "block_size": C2["bs"], "context": C2["ctx"],
-            "kv_pool_blocks": C2["pool_factor"] * C2["batch"] * C2["ctx"] // C2["bs"],
-            "l2": f"inputs rotate over {NUM_POOLS} KV pools ({NUM_POOLS * 2 * 2 * C2['batch'] * C2['ctx'] * C2['hkv'] * C2['d'] * 2 * C2['pool_factor'] // 2**20} MiB) > 3x L2",
-            "timing": "CUDA-graph replay of the public API launch, CUDA events, max over ranks",
-            "parallelism": f"request-sharded x{world} (no data-path collective)",
-        },
+        "config": c2_config(world),
+        "timing": "CUDA-graph replay of the public API launch, CUDA events on the launching "
+                  "stream, max over ranks",
         "roofline": {
             "bound": "hbm",
             "achieved": achieved,
@@ -396,7 +414,7 @@ def run_ours(args, rank, world, local_rank):
             "frac": achieved / peak,
             "traffic": _traffic_from_profile("paged_decode_c2_ctx2048"),
             "algorithmic_bytes_per_launch": nbytes,
-            "kernel": "fd::paged_decode_kernel<bf16,128,tma>",
+            "kernel": "fd::wave_decode_kernel<bf16,128,0,1,cluster,plain>",
         },
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -809,15 +827,16 @@ def run_sweep(torch, device, stream):
 # ---------------------------------------------------------------------------
 # CPU reference (the numpy oracle restating flashdec/paged_reference.py)
 # ---------------------------------------------------------------------------
-def _cpu_workload(seed=7):
+def _cpu_workload(seed=7, cfg=None):
     import numpy as np
 
     from tests.golden.cases import _normal
 
+    cfg = cfg or C2
     rng = np.random.default_rng(seed)
-    b, hq, hkv, d, bs, ctx = C2["batch"], C2["hq"], C2["hkv"], C2["d"], C2["bs"], C2["ctx"]
+    b, hq, hkv, d, bs, ctx = cfg["batch"], cfg["hq"], cfg["hkv"], cfg["d"], cfg["bs"], cfg["ctx"]
     nblk = ctx // bs
-    pool = C2["pool_factor"] * b * nblk
+    pool = cfg["pool_factor"] * b * nblk
     q = _normal(rng, (b, hq, d), "bfloat16")
     k = _normal(rng, (pool, hkv, bs, d), "bfloat16")
     v = _normal(rng, (pool, hkv, bs, d), "bfloat16")
@@ -826,36 +845,78 @@ def _cpu_workload(seed=7):
     return q, k, v, bt, sl
 
 
+def _c1_workload(seed=11):
+    """B=4, 16q/2kv, D128, bs32, fp32, seq U[64,512], a
+    seeded permutation of a 128-block pool, sm_scale 128^-0.5."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    b, hq, hkv, d, bs, nb = 4, 16, 2, 128, 32, 128
+    sl = rng.integers(64, 513, size=b).astype(np.int32)
+    maxblk = nb // b
+    bt = rng.permutation(nb)[: b * maxblk].reshape(b, maxblk).astype(np.int32)
+    q = rng.standard_normal((b, hq, d)).astype(np.float32)
+    k = rng.standard_normal((nb, hkv, bs, d)).astype(np.float32)
+    v = rng.standard_normal((nb, hkv, bs, d)).astype(np.float32)
+    return q, k, v, bt, sl
+
+
 # ---------------------------------------------------------------------------
-# CPU side: the oracle on every host core.  numpy's per-call overhead holds
-# the GIL, so threads do not scale; a process pool does.  It is started with
-# "spawn" (fresh interpreters), which is safe after CUDA is initialised.
-# Each worker builds the seeded workload itself and runs whole sequences.
+# CPU side.  The timed CPU path is the reference's own PyTorch
+# paged_decode_attention_ref (flashdec/paged_reference.py:19-125) from the
+# reference install under baseline/_ref when it is there ("reference"), else
+# the numpy oracle restating it ("port").  Sequences run one per task on a
+# process pool with one worker per host core (each worker limited to one
+# thread); the pool is started with "spawn" (fresh interpreters), which is
+# safe after CUDA is initialised.  Each worker builds the seeded workload
+# itself.
 # ---------------------------------------------------------------------------
+REF_DIR = REPO / "baseline" / "_ref"
 _POOL_WORK = None
+_POOL_FN = None
 
 
-def _pool_init():
-    global _POOL_WORK
+def _reference_available():
+    return (REF_DIR / "flashdec" / "paged_reference.py").exists()
+
+
+def _pool_init(kind, workload):
+    global _POOL_WORK, _POOL_FN
     try:
         from threadpoolctl import threadpool_limits
 
         threadpool_limits(limits=1)  # one core per worker
     except Exception:
         pass
-    _POOL_WORK = _cpu_workload()
+    arrays = _c1_workload() if workload == "c1" else _cpu_workload()
+    if kind == "reference":
+        import torch
+
+        torch.set_num_threads(1)
+        sys.path.insert(0, str(REF_DIR))
+        from flashdec.paged_reference import paged_decode_attention_ref
+
+        q, k, v, bt, sl = arrays
+        dt = torch.float32 if workload == "c1" else torch.bfloat16
+        _POOL_WORK = (torch.from_numpy(q).to(dt), torch.from_numpy(k).to(dt),
+                      torch.from_numpy(v).to(dt), torch.from_numpy(bt), torch.from_numpy(sl))
+        _POOL_FN = paged_decode_attention_ref
+    else:
+        from oracle import paged_decode_attention_ref
+
+        _POOL_WORK = arrays
+        dtype = "float32" if workload == "c1" else "bfloat16"
+        _POOL_FN = lambda q, k, v, bt, sl: paged_decode_attention_ref(q, k, v, bt, sl, dtype=dtype)
 
 
 def _pool_seq(i):
-    from oracle import paged_decode_attention_ref
-
     q, k, v, bt, sl = _POOL_WORK
     i %= q.shape[0]
-    paged_decode_attention_ref(q[i:i + 1], k, v, bt[i:i + 1], sl[i:i + 1], dtype="bfloat16")
+    _POOL_FN(q[i:i + 1], k, v, bt[i:i + 1], sl[i:i + 1])
     return i
 
 
-def _oracle_pool():
+def _cpu_pool(workload="c2"):
     import multiprocessing as mp
 
     try:
@@ -863,57 +924,75 @@ def _oracle_pool():
     except AttributeError:
         n = os.cpu_count() or 1
     n = max(1, min(n, 64))
-    pool = mp.get_context("spawn").Pool(n, initializer=_pool_init)
+    kind = "reference" if _reference_available() else "port"
+    pool = mp.get_context("spawn").Pool(n, initializer=_pool_init, initargs=(kind, workload))
     pool.map(_pool_seq, range(n))  # start-up (imports, workload) outside the timing
-    return pool, n
+    return pool, n, kind
 
 
-def _pool_sequences(pool, n, seconds, max_sequences=None):
-    """Run c2 sequences on the pool for about `seconds`; (sequences, elapsed)."""
+def _pool_sequences(pool, n, seconds):
+    """Run sequences on the pool for about `seconds`; (sequences, elapsed)."""
     done = 0
     t0 = time.perf_counter()
     while time.perf_counter() - t0 < seconds:
         chunk = 4 * n
-        if max_sequences is not None:
-            chunk = min(chunk, max_sequences - done)
-            if chunk <= 0:
-                break
         pool.map(_pool_seq, range(done, done + chunk))
         done += chunk
     return done, time.perf_counter() - t0
 
 
-def cpu_baseline_sample(args, seconds=None):
-    """Time the oracle on a bounded sample of the c2 workload (sequences) on
+_KIND_TEXT = {
+    "reference": "the reference's own PyTorch paged_decode_attention_ref "
+                 "(flashdec/paged_reference.py:19-125, installed under baseline/_ref)",
+    "port": "the numpy oracle restating flashdec/paged_reference.py:19-125 (no reference "
+            "install under baseline/_ref)",
+}
+
+
+def cpu_baseline_sample(args, seconds=None, workload="c2"):
+    """Time the CPU path on a bounded sample of the workload's sequences on
     all host cores."""
     seconds = seconds if seconds is not None else float(os.environ.get("FD_CPU_SECONDS", "10"))
-    pool, n = _oracle_pool()
+    pool, n, kind = _cpu_pool(workload)
     try:
         n_seq, dt = _pool_sequences(pool, n, seconds)
     finally:
         pool.close()
         pool.join()
+    what = ("c1 (B4, 16q/2kv, D128, bs32, fp32, seq U[64,512])" if workload == "c1"
+            else "c2 (ctx 2048, 16q/2kv, D128, bf16)")
     return {
         "value": n_seq / dt,
         "unit": "tokens/s",
         "cores": n,
-        "kind": "port",
-        "sample": f"{n_seq} sequences of the c2 workload (ctx 2048, 16q/2kv, D128) in {dt:.1f} s "
-                  f"on {n} worker processes (one core each), numpy oracle restating "
-                  "flashdec/paged_reference.py:19-125",
+        "kind": kind,
+        "sample": f"{n_seq} sequences of the {what} workload in {dt:.1f} s on {n} worker "
+                  f"processes (one core each), {_KIND_TEXT[kind]}",
+    }
+
+
+def c2_config(world):
+    """The `config` both arms report (same keys and values)."""
+    return {
+        "workload": "BASELINE c2: Qwen2.5-3B-shape paged decode attention, B8 ctx2048",
+        "batch_per_gpu": C2["batch"], "q_heads": C2["hq"], "kv_heads": C2["hkv"],
+        "head_dim": C2["d"], "block_size": C2["bs"], "context": C2["ctx"],
+        "kv_pool_blocks": C2["pool_factor"] * C2["batch"] * C2["ctx"] // C2["bs"],
+        "l2": f"inputs rotate over {NUM_POOLS} KV pools ({NUM_POOLS * 2 * 2 * C2['batch'] * C2['ctx'] * C2['hkv'] * C2['d'] * 2 * C2['pool_factor'] // 2**20} MiB) > 3x L2",
+        "parallelism": f"request-sharded x{world} (no data-path collective)",
     }
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    # per step: one full c2 batch (8 sequences) through the oracle, sequences
-    # spread over every host core; steps are capped so the run stays within a
-    # few minutes.
-    budget = float(os.environ.get("FD_REF_SECONDS", "60"))
-    pool, n = _oracle_pool()
+    # A step is one c2 batch (8 sequences) on the host cores; the sample is
+    # sized by time, not by --steps, so that the rate is not dominated by
+    # start-up (at least FD_REF_SECONDS, default 10 s).
+    budget = float(os.environ.get("FD_REF_SECONDS", "10"))
+    pool, n, kind = _cpu_pool("c2")
     try:
-        n_seq, dt = _pool_sequences(pool, n, budget, max_sequences=C2["batch"] * args.steps)
+        n_seq, dt = _pool_sequences(pool, n, budget)
     finally:
         pool.close()
         pool.join()
@@ -925,22 +1004,19 @@ def run_reference(args, rank, world):
         "value": value,
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": steps,
-        "steps_requested": args.steps,
+        "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * dt / steps,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16 inputs, fp32 math",
+        "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, scattered block tables)",
-        "config": {"workload": "BASELINE c2: Qwen2.5-3B-shape paged decode attention, B8 ctx2048",
-                   "device": "host CPU"},
+        "config": c2_config(world),
         "cpu_baseline": {
-            "value": value, "unit": "tokens/s", "cores": n, "kind": "port",
-            "sample": f"{n_seq} c2 sequences ({steps} steps of 8, capped at {budget:.0f} s) on {n} "
-                      "worker processes through the numpy oracle restating "
-                      "flashdec/paged_reference.py:19-125",
+            "value": value, "unit": "tokens/s", "cores": n, "kind": kind,
+            "sample": f"{n_seq} c2 sequences ({steps} batches of 8) in {dt:.1f} s on {n} worker "
+                      f"processes (one core each): {_KIND_TEXT[kind]}",
         },
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1000,9 +1076,12 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        # rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # rank 0 prints exactly one JSON line on stdout: NCCL's communicator
+        # set-up lines (INIT: ranks, devices, transports) go to stderr
+        if "NCCL_DEBUG" not in os.environ:
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))

@@ -2624,8 +2624,7 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
   const bool bf16 = a->dtype == FD_DTYPE_BF16;
   // Small batches (the balanced split plan) run as one wave of CTAs that fit
   // two per SM, so the next call's CTAs overlap this one (fd_wave_decode.cu).
-  if (tma && plan.balanced && !p.fused_append && !pre_pages &&
-      a->epilogue == FD_EPILOGUE_FUSED && wave_enabled()) {
+  if (tma && plan.balanced && !pre_pages && a->epilogue == FD_EPILOGUE_FUSED && wave_enabled()) {
     WaveParams w;
     std::memset(&w, 0, sizeof(w));
     w.num_seqs = p.num_seqs;
@@ -2674,6 +2673,25 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
     w.pss2 = p.pss2;
     w.tickets = p.tickets;
     w.status = p.status;
+    w.fused_append = p.fused_append;
+    w.ks3 = p.ks3;
+    w.vs3 = p.vs3;
+    w.ak = p.ak;
+    w.aks0 = p.aks0;
+    w.aks1 = p.aks1;
+    w.aks2 = p.aks2;
+    w.av = p.av;
+    w.avs0 = p.avs0;
+    w.avs1 = p.avs1;
+    w.avs2 = p.avs2;
+    w.slot = p.slot;
+    w.slot64 = p.slot64;
+    w.slots = p.slots;
+    w.rope_dim = p.rope_dim;
+    w.rope_inv_freq = p.rope_inv_freq;
+    w.rope_pos = p.rope_pos;
+    w.rope_pos64 = p.rope_pos64;
+    w.rope_pos_stride = p.rope_pos_stride;
     // head_dim 128: maps whose box is a whole page plane (the 32-token
     // maps above move one 64-dim half per box)
     CUtensorMap wk = mk, wv = mv;

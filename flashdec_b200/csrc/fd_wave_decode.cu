@@ -62,7 +62,7 @@ constexpr int kWaveBarConsumers = 1;  // named barrier of the consumer warps
 constexpr int kWavePrefetchPages = 64;
 // barriers (full, empty, cluster merge), tile masks, misc
 constexpr int kWaveCtlBytes = (kWaveTileBars + kWaveMaxStages + 2) * 8 + kWaveTileBars * 4 +
-                              kWaveMiscInts * 4;
+                              kWaveMiscInts * 4 + 2 * 64 * 4 + 2 * 128 * 2;
 // Shared-memory budget that keeps two CTAs resident per SM (228 KB per SM,
 // 1 KB reserved per CTA).
 constexpr size_t kWaveSmemBudget = 112 * 1024;
@@ -128,7 +128,7 @@ __device__ __forceinline__ uint32_t wave_page_rows(uint32_t pmask, int bs_shift)
   return m;
 }
 
-template <typename T, int D, int kPageRows, int kNT, bool kCluster>
+template <typename T, int D, int kPageRows, int kNT, bool kCluster, bool kAppend>
 __global__ void __launch_bounds__(kWaveThreads, 2)
     wave_decode_kernel(const __grid_constant__ WaveParams p,
                        const __grid_constant__ CUtensorMap tmap_k,
@@ -150,6 +150,11 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   uint64_t* merge_bar = empty_bar + kWaveMaxStages;
   uint32_t* tile_mask = reinterpret_cast<uint32_t*>(merge_bar + 2);
   int* misc = reinterpret_cast<int*>(tile_mask + kWaveTileBars);
+  // fused append: the appended token's slot (misc[4..5]), the cos / sin of
+  // its position per pair index, and its K (rotated) and V rows
+  int64_t* app_slot = reinterpret_cast<int64_t*>(misc + 4);
+  float* rope_tab = reinterpret_cast<float*>(misc + kWaveMiscInts);  // [2][64]
+  T* app_row = reinterpret_cast<T*>(rope_tab + 2 * 64);              // [2][D]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -257,7 +262,11 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   if (warp == kWaveProducerWarp) {
     const uint64_t policy = l2_policy_evict_first();
     int64_t n = 0;
-    if (lane == 0) n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
+    int64_t slotv = 0;
+    if (lane == 0) {
+      n = load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls);
+      if constexpr (kAppend) slotv = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
+    }
     // Block-table window (lane j: page wb + j; next window prefetched), first
     // placed where the prefetch warp's length says this CTA starts (or, when
     // its hint is not there yet, at the start for a full row); the real
@@ -277,10 +286,14 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     int win = bt_entry(wb + lane);
     int win_next = bt_entry(wb + 32 + lane);
     n = wave_clamp_len(p, __shfl_sync(0xffffffffu, n, 0));
+    // reference MASK_INVALID_SLOT: a negative slot attends to nothing
+    if (kAppend && __shfl_sync(0xffffffffu, slotv, 0) < 0) n = 0;
     const int tiles = static_cast<int>((n + kTile - 1) / kTile);
     int t0, t1;
     wave_range(split, S, tiles, t0, t1);
-    const int64_t nlb = (n + bs - 1) >> bs_shift;  // pages holding tokens
+    // pages holding cache tokens (with a fused append the last token comes
+    // from the call, not the cache)
+    const int64_t nlb = ((kAppend && n > 0 ? n - 1 : n) + bs - 1) >> bs_shift;
     const int ntile = t1 - t0;
     bool bad = false;
     const int ppt = 1 << ppt_shift;
@@ -367,7 +380,10 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   const int t4 = lane & 3;
   const int mi = lane >> 3;
   const int r8 = lane & 7;
-  const int64_t n = wave_clamp_len(p, load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls));
+  int64_t n = wave_clamp_len(p, load_index(p.sl, p.sl64, static_cast<int64_t>(b) * p.sls));
+  if constexpr (kAppend) {
+    if (load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots) < 0) n = 0;
+  }
   const int tiles = static_cast<int>((n + kTile - 1) / kTile);
   int t0, t1;
   wave_range(split, S, tiles, t0, t1);
@@ -391,7 +407,46 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     }
     *reinterpret_cast<uint4*>(qbuf + chunk_offset(row, ch)) = v;
   }
+  if constexpr (kAppend) {
+    // this sequence's new K / V row and its slot are staged with q (same
+    // memory round trip), so the tile that receives the row reads shared
+    // memory only
+    for (int e = tid; e < 2 * D; e += kWaveConsumerThreads) {
+      const int plane = e / D;
+      const int d = e - plane * D;
+      app_row[e] = plane ? static_cast<const T*>(p.av)[b * p.avs0 + kv_head * p.avs1 + d * p.avs2]
+                         : static_cast<const T*>(p.ak)[b * p.aks0 + kv_head * p.aks1 + d * p.aks2];
+    }
+    if (tid == 0) *app_slot = load_index(p.slot, p.slot64, static_cast<int64_t>(b) * p.slots);
+    if (tid < (p.rope_dim >> 1)) {
+      // cos / sin of this sequence's angles, once per pair index (the same
+      // for every q row and the K row; the RoPE + append kernel evaluates the
+      // same expression)
+      const float posf = static_cast<float>(
+          load_index(p.rope_pos, p.rope_pos64, static_cast<int64_t>(b) * p.rope_pos_stride));
+      float sn, cs;
+      sincosf(__fmul_rn(posf, p.rope_inv_freq[tid]), &sn, &cs);
+      rope_tab[tid] = cs;
+      rope_tab[64 + tid] = sn;
+    }
+  }
   named_barrier(kWaveBarConsumers, kWaveConsumerThreads);
+  if (kAppend && p.rope_dim > 0) {
+    // RoPE in place of the staged q rows and (row nrows) the appended K row:
+    // pair (i, i + rope_dim / 2)
+    const int half = p.rope_dim >> 1;
+    for (int e = tid; e < (nrows + 1) * half; e += kWaveConsumerThreads) {
+      const int row = e / half;
+      const int i = e - row * half;
+      T* x1p = row < nrows ? reinterpret_cast<T*>(qbuf + tile_offset(row, i)) : app_row + i;
+      T* x2p = row < nrows ? reinterpret_cast<T*>(qbuf + tile_offset(row, i + half)) : app_row + i + half;
+      float y1, y2;
+      rope_rotate_pair_cs(to_f32<T>(*x1p), to_f32<T>(*x2p), rope_tab[i], rope_tab[64 + i], y1, y2);
+      *x1p = from_f32<T>(y1);
+      *x2p = from_f32<T>(y2);
+    }
+    named_barrier(kWaveBarConsumers, kWaveConsumerThreads);
+  }
   // qf[nt][ks]: B fragment (k16 dims x n8 heads) of query heads nt * 8 + ..
   uint32_t qf[kNT][kKS][2];
   {
@@ -442,9 +497,19 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     const uint32_t kbase = smem_u32(sb);
     const uint32_t vbase = kbase + SM::kHalves * SM::kHalfBytes;
     // tokens of the tile that exist: pages present and position < n
-    const int64_t rem = n - static_cast<int64_t>(t) * kTile;
-    const uint32_t len_mask = rem >= 32 ? 0xffffffffu : ((1u << rem) - 1u);
-    const uint32_t vmask = wave_page_rows(tile_mask[i % kWaveTileBars], bs_shift) & len_mask;
+    // cache tokens of the tile that exist: pages present and position below
+    // the cache length (n, or n - 1 with a fused append)
+    const int64_t rem = (kAppend ? n - 1 : n) - static_cast<int64_t>(t) * kTile;
+    const uint32_t len_mask = rem >= 32 ? 0xffffffffu : (rem <= 0 ? 0u : ((1u << rem) - 1u));
+    uint32_t vmask = wave_page_rows(tile_mask[i % kWaveTileBars], bs_shift) & len_mask;
+    int ra = -1;  // row of the appended token in this tile
+    if constexpr (kAppend) {
+      const int64_t r = n - 1 - static_cast<int64_t>(t) * kTile;
+      if (r >= 0 && r < kTile) {
+        ra = static_cast<int>(r);
+        vmask |= 1u << ra;
+      }
+    }
     bool touched = false;
     if (vmask != 0xffffffffu) {
       // rows without data: zero V so that P (0 there) times V stays 0 even
@@ -461,6 +526,30 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       __syncwarp();
       touched = true;
     }
+    if (kAppend && ra >= 0) {
+      // current token: K / V from the call (K rotated with RoPE) patch the
+      // tile, and head block 0 stores them into the token's cache slot
+      // (reference paged_decode.py:193-221)
+      const int64_t slot = *app_slot;
+      const int64_t sblk = slot >> bs_shift;
+      const int64_t soff = slot - sblk * bs;
+      const bool store = jb == 0 && sblk < p.num_blocks;
+      T* kc = static_cast<T*>(const_cast<void*>(p.k)) + sblk * p.ks0 + kv_head * p.ks1 + soff * p.ks2;
+      T* vc = static_cast<T*>(const_cast<void*>(p.v)) + sblk * p.vs0 + kv_head * p.vs1 + soff * p.vs2;
+      for (int d = lane; d < D; d += 32) {
+        const T kv = app_row[d];
+        const T vv = app_row[D + d];
+        *reinterpret_cast<T*>(sb + stage_tile_offset<kPageRows>(ra, d)) = kv;
+        *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes + stage_tile_offset<kPageRows>(ra, d)) = vv;
+        if (store) {
+          kc[d * p.ks3] = kv;
+          vc[d * p.vs3] = vv;
+        }
+      }
+      if (!store && jb == 0 && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
+      __syncwarp();
+      touched = true;
+    }
 
     // ---- S^T = K Q^T (32 tokens x 8 kNT heads) ----
     float sa[kQA][2][kNT][4];
@@ -471,18 +560,43 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
 #pragma unroll
         for (int nt = 0; nt < kNT; ++nt)
           sa[qa][mt][nt][0] = sa[qa][mt][nt][1] = sa[qa][mt][nt][2] = sa[qa][mt][nt][3] = 0.f;
+    // An ldmatrix takes about a hundred cycles to return, an mma a few to
+    // issue: K fragments are loaded kKA k steps ahead of their mma (all of
+    // them up front for a group of up to 8 heads, where registers allow).
+    constexpr int kKA = kNT == 1 ? kKS : 2;
+    uint32_t ka[kKA][2][4];
+    auto load_k = [&](int ks, uint32_t (&dst)[2][4]) {
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        ldsm_x4(kbase + k_row + mt * SS::kRows16Bytes + (ks >> 2) * SS::kHalfStride + k_sw[ks & 3],
+                dst[mt][0], dst[mt][1], dst[mt][2], dst[mt][3]);
+      }
+    };
+#pragma unroll
+    for (int ks = 0; ks < kKA; ++ks) load_k(ks, ka[ks]);
 #pragma unroll
     for (int ks = 0; ks < kKS; ++ks) {
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        uint32_t a[4];
-        ldsm_x4(kbase + k_row + mt * SS::kRows16Bytes + (ks >> 2) * SS::kHalfStride + k_sw[ks & 3],
-                a[0], a[1], a[2], a[3]);
 #pragma unroll
         for (int nt = 0; nt < kNT; ++nt)
-          mma_16816<T>(sa[ks % kQA][mt][nt], a, qf[nt][ks][0], qf[nt][ks][1]);
+          mma_16816<T>(sa[ks % kQA][mt][nt], ka[ks % kKA][mt], qf[nt][ks][0], qf[nt][ks][1]);
       }
+      if (ks + kKA < kKS) load_k(ks + kKA, ka[ks % kKA]);
     }
+    // V fragments do not depend on the softmax: the first kVAhead (every one
+    // for a group of up to 8 heads) are issued now, under the softmax
+    constexpr int kVF = 2 * kMTD;  // V^T fragments of a tile: (token k step, dim m tile)
+    constexpr int kVAhead = kNT == 1 ? kVF : 4;
+    uint32_t va[kVAhead][4];
+    auto load_v = [&](int f, uint32_t (&dst)[4]) {
+      const int ks = f / kMTD;
+      const int mt = f - ks * kMTD;
+      ldsm_x4_t(vbase + v_row + ks * SS::kRows16Bytes + (mt >> 2) * SS::kHalfStride + v_sw[mt & 3],
+                dst[0], dst[1], dst[2], dst[3]);
+    };
+#pragma unroll
+    for (int f = 0; f < kVAhead; ++f) load_v(f, va[f]);
     float sc[2][kNT][4];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
@@ -566,15 +680,14 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
 
     // ---- O^T += V^T P^T ----
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
+    for (int f = 0; f < kVF; ++f) {
+      const int ks = f / kMTD;
+      const int mt = f - ks * kMTD;
+      uint32_t a[4] = {va[f % kVAhead][0], va[f % kVAhead][1], va[f % kVAhead][2],
+                       va[f % kVAhead][3]};
+      if (f + kVAhead < kVF) load_v(f + kVAhead, va[f % kVAhead]);
 #pragma unroll
-      for (int mt = 0; mt < kMTD; ++mt) {
-        uint32_t a[4];
-        ldsm_x4_t(vbase + v_row + ks * SS::kRows16Bytes + (mt >> 2) * SS::kHalfStride + v_sw[mt & 3],
-                  a[0], a[1], a[2], a[3]);
-#pragma unroll
-        for (int nt = 0; nt < kNT; ++nt) mma_16816<T>(o[mt][nt], a, pb[ks][nt][0], pb[ks][nt][1]);
-      }
+      for (int nt = 0; nt < kNT; ++nt) mma_16816<T>(o[mt][nt], a, pb[ks][nt][0], pb[ks][nt][1]);
     }
     __syncwarp();
     if (touched) fence_proxy_async_smem();
@@ -849,11 +962,11 @@ size_t wave_smem(int stages, int recv_bytes) {
          recv_bytes + kWaveCtlBytes;
 }
 
-template <typename T, int D, int kPageRows, int kNT, bool kCluster>
+template <typename T, int D, int kPageRows, int kNT, bool kCluster, bool kAppend>
 int wave_launch(WaveParams p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
                 const DeviceInfo& dev, cudaStream_t stream, bool* fits) {
   using SM = WaveSmem<D>;
-  auto kern = wave_decode_kernel<T, D, kPageRows, kNT, kCluster>;
+  auto kern = wave_decode_kernel<T, D, kPageRows, kNT, kCluster, kAppend>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   const int slot = dev.device & 63;
@@ -918,23 +1031,32 @@ int wave_launch(WaveParams p, const CUtensorMap& mk, const CUtensorMap& mv, dim3
 }
 
 // Cluster merge when it fits and the tickets are not needed, else the ticket merge.
-template <typename T, int D, int kPageRows, int kNT>
+template <typename T, int D, int kPageRows, int kNT, bool kAppend>
 int wave_merge_kind(const WaveParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
                     const DeviceInfo& dev, cudaStream_t stream) {
   bool fits = false;
   if (grid.x >= 2 && cluster_enabled()) {
-    const int rc = wave_launch<T, D, kPageRows, kNT, true>(p, mk, mv, grid, dev, stream, &fits);
+    const int rc =
+        wave_launch<T, D, kPageRows, kNT, true, kAppend>(p, mk, mv, grid, dev, stream, &fits);
     if (fits) return rc;
   }
   if (grid.x >= 2 && (!p.pacc || !p.tickets)) return FD_ERR_UNSUPPORTED;
-  return wave_launch<T, D, kPageRows, kNT, false>(p, mk, mv, grid, dev, stream, &fits);
+  return wave_launch<T, D, kPageRows, kNT, false, kAppend>(p, mk, mv, grid, dev, stream, &fits);
+}
+
+template <typename T, int D, int kPageRows, int kNT>
+int wave_append(const WaveParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
+                const DeviceInfo& dev, cudaStream_t stream) {
+  // the fused append is its own instantiation: the plain decode carries none of its code
+  return p.fused_append ? wave_merge_kind<T, D, kPageRows, kNT, true>(p, mk, mv, grid, dev, stream)
+                        : wave_merge_kind<T, D, kPageRows, kNT, false>(p, mk, mv, grid, dev, stream);
 }
 
 template <typename T, int D, int kPageRows>
 int wave_rows(const WaveParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
               const DeviceInfo& dev, cudaStream_t stream) {
-  return p.rows <= 8 ? wave_merge_kind<T, D, kPageRows, 1>(p, mk, mv, grid, dev, stream)
-                     : wave_merge_kind<T, D, kPageRows, 2>(p, mk, mv, grid, dev, stream);
+  return p.rows <= 8 ? wave_append<T, D, kPageRows, 1>(p, mk, mv, grid, dev, stream)
+                     : wave_append<T, D, kPageRows, 2>(p, mk, mv, grid, dev, stream);
 }
 
 template <typename T>

@@ -47,6 +47,26 @@ struct WaveParams {
   int64_t pss0, pss1, pss2;
   int* tickets;  // one per (sequence, head block) pair, zero between calls
   int* status;
+  // fused current-token append (the reference vLLM launcher's
+  // paged_decode.py:193-221): token seq_len - 1 of every sequence comes from
+  // append_k / append_v [seq, kv_head, dim] instead of the cache and is
+  // stored at slot_mapping[seq]; a negative slot gives a zero output and no
+  // store.  With rope_dim > 0 the q rows and the appended K row are rotated
+  // by rope_positions[seq] with the fp32 table rope_inv_freq[rope_dim / 2].
+  int fused_append;
+  int64_t ks3, vs3;  // dim strides of the caches (stores)
+  const void* ak;
+  int64_t aks0, aks1, aks2;
+  const void* av;
+  int64_t avs0, avs1, avs2;
+  const void* slot;
+  int slot64;
+  int64_t slots;
+  int rope_dim;
+  const float* rope_inv_freq;
+  const void* rope_pos;
+  int rope_pos64;
+  int64_t rope_pos_stride;
 };
 
 // Whether fd_paged_decode may use the one-wave kernel for small batches
