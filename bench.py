@@ -152,10 +152,9 @@ def c2_bytes():
 
 
 def ragged_requests(seed=4, batch=64):
-    import numpy as np
+    from tests.golden.cases import c4_lengths
 
-    rng = np.random.default_rng(seed)
-    return [int(x) for x in np.exp(rng.uniform(np.log(512), np.log(131072), size=batch))]
+    return c4_lengths(seed, batch)
 
 
 # ---------------------------------------------------------------------------

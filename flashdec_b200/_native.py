@@ -64,43 +64,71 @@ def index_ranges(*tensors):
 
 
 # --------------------------------------------------------------------------
-# workspace: a zero-filled int32 ticket array (the kernel leaves it zero) and
-# fp32 scratch, per device, grown on demand and reused by every call on that
-# device.  Calls that share it must be ordered on one stream.
+# workspace: a zero-filled int32 ticket array (the kernels leave it zero) and
+# fp32 scratch, grown on demand.  Every stream gets its own pair, so calls
+# that overlap on the GPU (on different streams) never share tickets or
+# partials; calls on one stream are ordered and share theirs.  A stream first
+# seen during CUDA graph capture cannot allocate: it uses the device's default
+# pair, which reserve_workspace pre-sizes and every eager call keeps at least
+# as large as its own need (graphs replayed concurrently on several streams
+# should therefore each be captured after an eager call on their stream).
 # --------------------------------------------------------------------------
 class _Workspace:
     def __init__(self):
         self.tickets = None
         self.scratch = None
 
+    def fits(self, tickets_needed, scratch_bytes):
+        return ((tickets_needed <= 0 or (self.tickets is not None
+                                         and self.tickets.numel() >= tickets_needed))
+                and (scratch_bytes <= 0 or (self.scratch is not None
+                                            and self.scratch.numel() * 4 >= scratch_bytes)))
+
+    def grow(self, device, tickets_needed, scratch_bytes):
+        if tickets_needed > 0 and (self.tickets is None or self.tickets.numel() < tickets_needed):
+            cap = max(1024, 1 << math.ceil(math.log2(tickets_needed)))
+            self.tickets = torch.zeros(cap, dtype=torch.int32, device=device)
+        if scratch_bytes > 0 and (self.scratch is None or self.scratch.numel() * 4 < scratch_bytes):
+            n = max(1 << 16, 1 << math.ceil(math.log2((scratch_bytes + 3) // 4)))
+            self.scratch = torch.empty(n, dtype=torch.float32, device=device)
+
 
 _ws_lock = threading.Lock()
-_ws: dict[int, _Workspace] = {}
+_ws: dict = {}  # (device index, stream handle or None for the default) -> _Workspace
 
 
-def workspace(device: torch.device, tickets_needed: int, scratch_bytes: int):
+def workspace(device: torch.device, tickets_needed: int, scratch_bytes: int, stream=None):
+    """(tickets, scratch) for calls on `stream` (a raw handle; default: the
+    current stream of `device`)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    if stream is None:
+        stream = stream_handle(idx)
     with _ws_lock:
-        ws = _ws.setdefault(idx, _Workspace())
-        grow_t = tickets_needed > 0 and (ws.tickets is None or ws.tickets.numel() < tickets_needed)
-        grow_s = scratch_bytes > 0 and (ws.scratch is None or ws.scratch.numel() * 4 < scratch_bytes)
-        if (grow_t or grow_s) and torch.cuda.is_current_stream_capturing():
+        ws = _ws.get((idx, stream))
+        if ws is not None and ws.fits(tickets_needed, scratch_bytes):
+            return ws.tickets, ws.scratch
+        default = _ws.setdefault((idx, None), _Workspace())
+        if torch.cuda.is_current_stream_capturing():
+            if ws is None and default.fits(tickets_needed, scratch_bytes):
+                return default.tickets, default.scratch
             raise RuntimeError(
                 "flashdec_b200 workspace must grow during CUDA graph capture; run one eager "
                 "call with the largest batch first (or call reserve_workspace)"
             )
-        if grow_t:
-            cap = max(1024, 1 << math.ceil(math.log2(tickets_needed)))
-            ws.tickets = torch.zeros(cap, dtype=torch.int32, device=device)
-        if grow_s:
-            n = max(1 << 16, 1 << math.ceil(math.log2((scratch_bytes + 3) // 4)))
-            ws.scratch = torch.empty(n, dtype=torch.float32, device=device)
+        if ws is None:
+            ws = _ws[(idx, stream)] = _Workspace()
+        ws.grow(device, tickets_needed, scratch_bytes)
+        default.grow(device, tickets_needed, scratch_bytes)  # fallback for capture
         return ws.tickets, ws.scratch
 
 
 def reserve_workspace(device, tickets: int, scratch_bytes: int) -> None:
-    """Pre-size the per-device workspace (call before CUDA graph capture)."""
-    workspace(torch.device(device), tickets, scratch_bytes)
+    """Pre-size the device's default workspace (call before CUDA graph
+    capture on streams that have made no eager call)."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        _ws.setdefault((idx, None), _Workspace()).grow(device, tickets, scratch_bytes)
 
 
 # --------------------------------------------------------------------------
@@ -109,21 +137,41 @@ def reserve_workspace(device, tickets: int, scratch_bytes: int) -> None:
 class PreparedDecode:
     """``fd_paged_decode`` arguments prepared once for one call signature
     (shapes, strides, dtypes, scalars) together with the workspace they
-    point at; :meth:`launch` only sets the data pointers.  A lock keeps two
+    point at; :meth:`launch` only sets the data pointers (and, on a stream it
+    has not launched on before, that stream's workspace).  A lock keeps two
     threads from interleaving on the shared struct (ctypes releases the GIL
     during the foreign call)."""
 
-    __slots__ = ("lib", "args", "workspace", "lock")
+    __slots__ = ("lib", "args", "device", "need", "stream", "per_stream", "lock")
 
-    def __init__(self, lib, args, workspace):
+    def __init__(self, lib, args, device, need, stream, ws):
         self.lib = lib
         self.args = args
-        self.workspace = workspace  # held: a later workspace growth cannot free it
+        self.device = device
+        self.need = need  # (tickets, scratch bytes)
+        self.stream = stream
+        # stream -> (tickets, scratch) held, so a later growth cannot free them
+        self.per_stream = {stream: ws}
         self.lock = threading.Lock()
+
+    def _bind(self, stream):
+        ws = self.per_stream.get(stream)
+        if ws is None:
+            ws = workspace(self.device, self.need[0], self.need[1], stream)
+            self.per_stream[stream] = ws
+        tickets, scratch = ws
+        a = self.args
+        if tickets is not None:
+            a.tickets, a.tickets_capacity = tickets.data_ptr(), tickets.numel()
+        if scratch is not None:
+            a.scratch, a.scratch_bytes = scratch.data_ptr(), scratch.numel() * 4
+        self.stream = stream
 
     def launch(self, q, k, v, block_tables, seq_lens, out, stream):
         a = self.args
         with self.lock:
+            if stream != self.stream and (self.need[0] or self.need[1]):
+                self._bind(stream)
             a.q, a.out = q.data_ptr(), out.data_ptr()
             a.k_cache, a.v_cache = k.data_ptr(), v.data_ptr()
             a.block_tables, a.seq_lens = block_tables.data_ptr(), seq_lens.data_ptr()
@@ -202,15 +250,18 @@ def prepare_paged_decode(q, k4, v4, block_tables, seq_lens, out, *, sm_scale, bl
                                              ctypes.byref(tickets_needed)),
                "fd_paged_decode_workspace")
     ws = (None, None)
+    stream = stream_handle(q.device)
     if scratch_bytes.value or tickets_needed.value:
-        ws = tickets, scratch = workspace(q.device, tickets_needed.value, scratch_bytes.value)
+        ws = tickets, scratch = workspace(q.device, tickets_needed.value, scratch_bytes.value,
+                                          stream)
         if tickets is not None:
             a.tickets = tickets.data_ptr()
             a.tickets_capacity = tickets.numel()
         if scratch is not None:
             a.scratch = scratch.data_ptr()
             a.scratch_bytes = scratch.numel() * 4
-    return PreparedDecode(lib, a, ws)
+    return PreparedDecode(lib, a, q.device, (tickets_needed.value, scratch_bytes.value), stream,
+                          ws)
 
 
 def paged_decode(q, k4, v4, block_tables, seq_lens, out, **kw):

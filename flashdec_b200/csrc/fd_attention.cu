@@ -2696,7 +2696,22 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
     // maps above move one 64-dim half per box)
     CUtensorMap wk = mk, wv = mv;
     bool wtma = true;
+    w.num_kv_heads = a->num_kv_heads;
     if (D == 128 && a->block_size == 32) {
+      // a contiguous token-major pair of caches: one box per page moves K and V
+      CacheDesc cd;
+      cd.base = a->k_cache;
+      cd.elem_bytes = 2;
+      cd.is_bf16 = a->dtype == FD_DTYPE_BF16;
+      cd.head_dim = D;
+      cd.block_size = a->block_size;
+      cd.num_heads = a->num_kv_heads;
+      cd.num_blocks = a->num_blocks;
+      for (int i = 0; i < 4; ++i) cd.stride[i] = a->k_stride[i];
+      w.kv_box = kv_pair_enabled() &&
+                 get_kv_pair_tensor_map(cd, a->v_cache, a->v_stride, &wk, &w.v_first);
+    }
+    if (D == 128 && a->block_size == 32 && !w.kv_box) {
       for (int plane = 0; plane < 2 && wtma; ++plane) {
         CacheDesc cd;
         cd.base = plane ? a->v_cache : a->k_cache;

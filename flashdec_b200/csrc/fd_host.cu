@@ -64,8 +64,28 @@ struct MapEntry {
   uint64_t stamp;
 };
 
+// K + V pair maps (get_kv_pair_tensor_map)
+struct PairKey {
+  const void* k;
+  const void* v;
+  int is_bf16, num_heads, num_blocks;
+  int64_t stride[4];
+  bool operator==(const PairKey& o) const {
+    return k == o.k && v == o.v && is_bf16 == o.is_bf16 && num_heads == o.num_heads &&
+           num_blocks == o.num_blocks && std::memcmp(stride, o.stride, sizeof(stride)) == 0;
+  }
+};
+
+struct PairEntry {
+  PairKey key;
+  CUtensorMap map;
+  int v_first;
+  uint64_t stamp;
+};
+
 std::mutex g_map_mu;
 std::vector<MapEntry> g_maps;
+std::vector<PairEntry> g_pairs;
 uint64_t g_map_clock = 0;
 constexpr size_t kMapCacheSize = 64;
 
@@ -125,6 +145,14 @@ bool cascade_concurrent_enabled() {
 bool cluster_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("FLASHDEC_B200_CLUSTER");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+bool kv_pair_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLASHDEC_B200_KV_PAIR");
     return !(v && v[0] == '0');
   }();
   return on;
@@ -234,6 +262,70 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
   }
   *out = map;
   std::copy(pm, pm + 4, perm);
+  return true;
+}
+
+bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_t v_stride[4],
+                            CUtensorMap* out, int* v_first) {
+  if (k.elem_bytes != 2 || k.head_dim != 128 || k.block_size != 32) return false;
+  for (int i = 0; i < 4; ++i)
+    if (k.stride[i] != v_stride[i]) return false;
+  if (k.stride[3] != 1) return false;
+  // planes (block, head) evenly spaced: a single plane index blk * heads + head
+  const int64_t plane = k.num_heads == 1 ? k.stride[0] : k.stride[1];
+  if (k.num_heads > 1 && k.stride[0] != plane * k.num_heads) return false;
+  const int64_t tok_bytes = k.stride[2] * 2;
+  const int64_t plane_bytes = plane * 2;
+  if (tok_bytes % 16 || plane_bytes % 16 || tok_bytes <= 0 || plane_bytes <= 0) return false;
+  const uintptr_t kb = reinterpret_cast<uintptr_t>(k.base);
+  const uintptr_t vb = reinterpret_cast<uintptr_t>(v_base);
+  if (kb % 16 || vb % 16 || kb == vb) return false;
+  const uintptr_t lo = kb < vb ? kb : vb;
+  const uint64_t delta = kb < vb ? vb - kb : kb - vb;
+  if (delta % 16 || delta >= (uint64_t(1) << 40)) return false;
+  const int64_t planes = static_cast<int64_t>(k.num_blocks) * k.num_heads;
+  // the plane axis must not reach into the other allocation's range: one
+  // allocation's last plane ends before the other starts (delta covers it)
+  if (static_cast<uint64_t>(planes) * plane_bytes > delta) return false;
+  PairKey key{k.base, v_base, k.is_bf16, k.num_heads, k.num_blocks,
+              {k.stride[0], k.stride[1], k.stride[2], k.stride[3]}};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    for (auto& e : g_pairs) {
+      if (e.key == key) {
+        e.stamp = ++g_map_clock;
+        *out = e.map;
+        *v_first = e.v_first;
+        return true;
+      }
+    }
+  }
+  resolve_encoder();
+  if (!g_encode) return false;
+  cuuint64_t dims[5] = {64u, 32u, 2u, static_cast<cuuint64_t>(planes), 2u};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(tok_bytes), 128u,
+                           static_cast<cuuint64_t>(plane_bytes), static_cast<cuuint64_t>(delta)};
+  cuuint32_t box[5] = {64u, 32u, 2u, 1u, 2u};
+  cuuint32_t estride[5] = {1u, 1u, 1u, 1u, 1u};
+  CUtensorMap map;
+  const CUresult r = g_encode(&map,
+                              k.is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              5u, reinterpret_cast<void*>(lo), dims, strides, box, estride,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  *out = map;
+  *v_first = vb < kb ? 1 : 0;
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  if (g_pairs.size() >= kMapCacheSize) {
+    auto oldest = std::min_element(g_pairs.begin(), g_pairs.end(),
+                                   [](const PairEntry& a, const PairEntry& b) {
+                                     return a.stamp < b.stamp;
+                                   });
+    g_pairs.erase(oldest);
+  }
+  g_pairs.push_back(PairEntry{key, map, *v_first, ++g_map_clock});
   return true;
 }
 

@@ -47,6 +47,17 @@ struct CacheDesc {
 // be described by a tensor map.
 bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]);
 
+// One tensor map over both planes of a pair of caches with head_dim 128 and
+// 32-token pages whose (block, head) planes are contiguous and evenly spaced
+// (block stride = heads x head stride, unit dim stride): dims [64 dims, 32
+// tokens, 2 halves, block * heads + head, 2 (K, V)] with the last axis
+// spanning the two allocations (stride |v - k|), box [64, 32, 2, 1, 2], 128B
+// swizzle.  One copy then moves a page's K and V (16 KB) as [plane][half]
+// [32 tokens][64 dims]; *v_first is set when V's allocation comes first
+// (plane 0 is V).  Returns false when the layout does not qualify.
+bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_t v_stride[4],
+                            CUtensorMap* out, int* v_first);
+
 // FD_OK, or FD_ERR_CUDA with the message kept for fd_error_string.
 int cuda_status(cudaError_t e);
 
@@ -61,6 +72,11 @@ bool pdl_enabled();
 // clusters (default on; FLASHDEC_B200_CLUSTER=0 turns it off and keeps the
 // global-memory ticket merge).
 bool cluster_enabled();
+
+// Whether the one-wave decode may move a page's K and V with one box through
+// a K + V pair map (default on; FLASHDEC_B200_KV_PAIR=0 keeps one box per
+// plane).
+bool kv_pair_enabled();
 
 // Whether the cascade prefix pass runs on tcgen05 UMMA where it can (head_dim
 // 128, 32-token pages; default on; FLASHDEC_B200_PREFIX_UMMA=0 keeps the

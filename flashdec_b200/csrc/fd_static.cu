@@ -21,8 +21,16 @@
 // initial value.
 //
 // Set-up: the first call on a device, with that device current, looks up the
-// arrays' device addresses (cudaGetSymbolAddress) and caches them per device.
-// Make that first call before any stream capture.
+// arrays' device addresses (cudaGetSymbolAddress) and caches them per device
+// together with the id of the device's current context; a call that finds a
+// different context (after cudaDeviceReset, which reloads the module and may
+// move the arrays) looks them up again.  Make the first call on a device, and
+// the first call after a reset, before any stream capture.
+//
+// Partials: with FD_EPILOGUE_PARTIALS the split partials must go to the
+// caller's part_acc / part_max / part_sum (the static scratch is private, so
+// the caller could not read them): a NULL part_acc is rejected with
+// FD_ERR_INVALID_ARGUMENT before anything else happens.
 //
 // Overlap: every call on a device shares the same storage.  Calls whose
 // execution overlaps on the GPU (different streams, or threads without an
@@ -34,6 +42,8 @@
 // tickets/scratch fields of the caller's arguments are ignored.
 #include <cstdint>
 #include <mutex>
+
+#include <cudaTypedefs.h>
 
 #include "../../include/flashdec_b200.h"
 #include "fd_host.h"
@@ -54,10 +64,36 @@ namespace {
 struct StaticStorage {
   float* scratch = nullptr;
   int32_t* tickets = nullptr;
+  unsigned long long ctx_id = 0;  // context the addresses belong to
 };
 
 std::mutex g_static_mu;
 StaticStorage g_static[kMaxDevices];
+
+// Id of the calling thread's current context (driver entry points resolved at
+// run time, no link-time libcuda dependency); 0 if it cannot be read.
+unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 // Device addresses of the static arrays on the current device (looked up on
 // the first call per device).
@@ -66,9 +102,10 @@ int static_storage(StaticStorage* out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fd::cuda_status(e);
   if (dev < 0 || dev >= kMaxDevices) return FD_ERR_UNSUPPORTED;
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_static_mu);
   StaticStorage& s = g_static[dev];
-  if (!s.scratch) {
+  if (!s.scratch || s.ctx_id != ctx) {
     void* scratch = nullptr;
     void* tickets = nullptr;
     e = cudaGetSymbolAddress(&scratch, fd_static_scratch);
@@ -77,6 +114,7 @@ int static_storage(StaticStorage* out) {
     if (e != cudaSuccess) return fd::cuda_status(e);
     s.tickets = static_cast<int32_t*>(tickets);
     s.scratch = static_cast<float*>(scratch);
+    s.ctx_id = ctx;
   }
   *out = s;
   return FD_OK;
@@ -85,6 +123,8 @@ int static_storage(StaticStorage* out) {
 }  // namespace
 
 extern "C" int fd_paged_decode_static(const fd_paged_decode_args* a, void* cuda_stream) {
+  // partials the caller asked for must land in the caller's buffers
+  if (a && a->epilogue == FD_EPILOGUE_PARTIALS && !a->part_acc) return FD_ERR_INVALID_ARGUMENT;
   size_t need_scratch = 0;
   int64_t need_tickets = 0;
   int rc = fd_paged_decode_workspace(a, &need_scratch, &need_tickets);

@@ -215,10 +215,10 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     const int64_t pg0 = static_cast<int64_t>(t0) << ppt_shift;
     int64_t pg1 = min(static_cast<int64_t>(t1) << ppt_shift, nlb);
     pg1 = min(pg1, pg0 + kWavePrefetchPages);
-    // block ids first (one per lane), then every 128-byte line of each
-    // page's K and V rows with all 32 lanes (one warp instruction covers 32
-    // lines), through the load unit: the TMA unit is left to the loads,
-    // whose every operation costs issue time on the SM
+    // block ids first (one per lane), then each page: one TMA prefetch of
+    // its K and V planes through the pair map when there is one, else every
+    // 128-byte line of its K and V rows with all 32 lanes (one warp
+    // instruction covers 32 lines) through the load unit
     constexpr int kLinesPerRow = D * 2 / 128;
     const int lines = bs * kLinesPerRow;  // lines of one page plane
     for (int64_t lb0 = pg0; lb0 < pg1; lb0 += 32) {
@@ -229,6 +229,14 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       for (int j = 0; j < npg; ++j) {
         const int64_t bj = __shfl_sync(0xffffffffu, blk, j);
         if (bj < 0 || bj >= p.num_blocks) continue;  // warp-uniform
+        if (p.kv_box) {
+          // one TMA prefetch per page through the K + V pair map (cheaper to
+          // issue than 256 line prefetches)
+          if (lane == 0) {
+            tma_prefetch_5d(&tmap_k, 0, 0, 0, static_cast<int>(bj) * p.num_kv_heads + kv_head, 0);
+          }
+          continue;
+        }
         const char* kp = static_cast<const char*>(p.k) + (bj * p.ks0 + kv_head * p.ks1) * 2;
         const char* vp = static_cast<const char*>(p.v) + (bj * p.vs0 + kv_head * p.vs1) * 2;
         for (int e = lane; e < lines; e += 32) {
@@ -341,7 +349,19 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       if (!__all_sync(0xffffffffu, ok)) break;
       // one box per (page, plane): a page's tokens x all of head_dim (the
       // head_dim 128 map carries the 64-dim half axis), [half][tokens][64]
-      // in the stage
+      // in the stage; with the K + V pair map one box per page moves both
+      // planes
+      if (D == 128 && kPageRows == 0 && p.kv_box) {
+        const int pblk = blk_l;  // lane = page of the group
+        if (lane < np && ((pages >> lane) & 1u)) {
+          const int i = i0 + (lane >> ppt_shift);
+          tma_load_5d(smem_u32(stages + (i % NST) * SM::kStageBytes), &tmap_k,
+                      smem_u32(&full_bar[i % kWaveTileBars]), 0, 0, 0,
+                      pblk * p.num_kv_heads + kv_head, 0, policy);
+        }
+        i0 += ng;
+        continue;
+      }
       const int nops = np * 2;
       for (int base = 0; base < nops; base += 32) {
         const int op = base + lane;
@@ -461,6 +481,11 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     }
   }
 
+  // Every CTA of the cluster arrived on the cluster barrier at its start, so
+  // this wait costs nothing here; it makes the peers' merge barriers (and
+  // receive areas) safe targets for the pushes at the end.
+  if constexpr (kCluster) cluster_wait();
+
   // Per-lane ldmatrix offsets in a stage (the same for every tile).  K as
   // the A operand (tokens x dims): row (mi & 1) * 8 + r8 (+16 per m tile),
   // chunk 2 (ks % 4) + (mi >> 1) of half ks / 4.  V^T as the A operand
@@ -475,6 +500,9 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     v_sw[j] = static_cast<uint32_t>((((2 * j) + (mi & 1)) ^ r8) << 4);
   }
 
+  // K and V regions of a stage (swapped when the pair map's first plane is V)
+  const uint32_t koff = (p.kv_box && p.v_first) ? SM::kHalves * SM::kHalfBytes : 0u;
+  const uint32_t voff = SM::kHalves * SM::kHalfBytes - koff;
   float m_run[kNT][2], l_run[kNT][2];
   // o[mt][nt][2 hf + e]: O^T[dim 16 mt + g8 + 8 hf][head nt * 8 + 2 t4 + e]
   float o[kMTD][kNT][4];
@@ -494,8 +522,8 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       continue;
     }
     uint8_t* sb = stages + stage * SM::kStageBytes;
-    const uint32_t kbase = smem_u32(sb);
-    const uint32_t vbase = kbase + SM::kHalves * SM::kHalfBytes;
+    const uint32_t kbase = smem_u32(sb) + koff;
+    const uint32_t vbase = smem_u32(sb) + voff;
     // tokens of the tile that exist: pages present and position < n
     // cache tokens of the tile that exist: pages present and position below
     // the cache length (n, or n - 1 with a fused append)
@@ -519,8 +547,8 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
         const int r = e / (D / 8);
         const int c = e - r * (D / 8);
         if ((inv >> r) & 1u) {
-          *reinterpret_cast<uint4*>(sb + SM::kHalves * SM::kHalfBytes +
-                                    stage_chunk_offset<kPageRows>(r, c)) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(sb + voff + stage_chunk_offset<kPageRows>(r, c)) =
+              make_uint4(0u, 0u, 0u, 0u);
         }
       }
       __syncwarp();
@@ -539,8 +567,8 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       for (int d = lane; d < D; d += 32) {
         const T kv = app_row[d];
         const T vv = app_row[D + d];
-        *reinterpret_cast<T*>(sb + stage_tile_offset<kPageRows>(ra, d)) = kv;
-        *reinterpret_cast<T*>(sb + SM::kHalves * SM::kHalfBytes + stage_tile_offset<kPageRows>(ra, d)) = vv;
+        *reinterpret_cast<T*>(sb + koff + stage_tile_offset<kPageRows>(ra, d)) = kv;
+        *reinterpret_cast<T*>(sb + voff + stage_tile_offset<kPageRows>(ra, d)) = vv;
         if (store) {
           kc[d * p.ks3] = kv;
           vc[d * p.vs3] = vv;
@@ -744,7 +772,6 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   float* recv = reinterpret_cast<float*>(rbuf);
   float2* recv_ml = reinterpret_cast<float2*>(recv + S * ri * D);
   const int crank = kCluster ? static_cast<int>(cluster_ctarank()) : 0;
-  if constexpr (kCluster) cluster_wait();  // every peer's receive area is free
 
   for (int u = tid; u < nrows * kUnits; u += kWaveConsumerThreads) {
     const int r = u / kUnits;

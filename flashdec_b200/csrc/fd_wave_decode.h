@@ -26,6 +26,9 @@ struct WaveParams {
   void* out;
   int64_t os0, os1, os2;
   int kperm[4], vperm[4];  // tensor-map axis order (0 token, 1 head, 2 block, 3 half)
+  // kv_box: the K map is a K + V pair map (get_kv_pair_tensor_map) and one
+  // box moves a page's K and V; v_first: V's plane comes first in the stage
+  int kv_box, v_first, num_kv_heads;
   // the caches (unit dim stride) for the L2 prefetch of the next call's pages
   const void* k;
   int64_t ks0, ks1, ks2;

@@ -197,7 +197,11 @@ int fd_cascade_decode(const fd_paged_decode_args* args, const fd_cascade_args* c
  * library (the tickets/scratch fields of `args` are ignored), for callers
  * that cannot allocate device memory.  No counterpart in the reference.
  * - The first call on a device (that device current) looks up the storage
- *   address; make it before any stream capture.
+ *   address, and so does the first call after the device's context changed
+ *   (cudaDeviceReset); make those calls before any stream capture.
+ * - FD_EPILOGUE_PARTIALS needs the caller's part_acc / part_max / part_sum
+ *   (the static scratch is private): a NULL part_acc returns
+ *   FD_ERR_INVALID_ARGUMENT.
  * - The tickets start at zero (zero-filled at module load) and every
  *   completed call leaves them at zero; after a call that raised
  *   FD_STATUS_WAIT_TIMEOUT, do not use this entry point again.

@@ -22,6 +22,12 @@ def _normal(rng, shape, dtype):
     return round_to_dtype(rng.standard_normal(shape, dtype=np.float32), dtype)
 
 
+def c4_lengths(seed=4, batch=64):
+    """BASELINE config 4's request lengths: log-uniform in [512, 131072]."""
+    rng = np.random.default_rng(seed)
+    return [int(x) for x in np.exp(rng.uniform(np.log(512), np.log(131072), size=batch))]
+
+
 # --------------------------------------------------------------------------
 # paged decode attention
 # --------------------------------------------------------------------------

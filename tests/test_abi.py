@@ -132,6 +132,10 @@ def test_host_argument_checks_answer_without_a_gpu(lib):
     assert lib.fd_cascade_decode(ctypes.byref(a), ctypes.byref(c), None) == \
         _lib.FD_ERR_INVALID_ARGUMENT
     assert lib.fd_cascade_decode(ctypes.byref(a), None, None) == _lib.FD_ERR_INVALID_ARGUMENT
+    # the entry point without allocation cannot hand back partials it would
+    # keep in its private static scratch: PARTIALS needs the caller's part_acc
+    a.num_splits, a.epilogue = 2, _lib.FD_EPILOGUE_PARTIALS
+    assert lib.fd_paged_decode_static(ctypes.byref(a), None) == _lib.FD_ERR_INVALID_ARGUMENT
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):

@@ -94,3 +94,45 @@ def test_gather_outputs_two_gloo_ranks(dst):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results == {0: True, 1: True}
+
+
+def _c4_worker(rank, world, port, result_q):
+    """LPT shards of BASELINE c4's 64 requests, each rank holding only its
+    rows, reassembled on every rank by the gather."""
+    import torch.distributed as dist
+
+    from tests.golden.cases import c4_lengths
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lens = c4_lengths()
+        shards = lpt_partition(lens, world)
+        hq, d = 32, 4
+        # row r carries the request's own index and length: the gather must
+        # put every row back at its request's position
+        full = torch.zeros(len(lens), hq, d)
+        for r, n in enumerate(lens):
+            full[r, :, 0] = r
+            full[r, :, 1] = n
+        out = gather_outputs(full[shards[rank]], shards, rank)
+        loads = shard_loads(lens, shards)
+        ok = torch.equal(out, full) and max(loads) <= 4 / 3 * max(sum(lens) / world, max(lens))
+        result_q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_c4_shards_and_gather_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_c4_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True}
