@@ -365,6 +365,7 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
     if world == 1 and not args.kernel_only:
         extra["c2_ctx1024"] = run_c2_ctx1024(torch, device, stream, args)
         extra["c3_rope_append"] = run_c3(torch, device, stream)
+        extra["vllm_launcher"] = run_vllm_launcher(torch, device, stream)
         extra["c5_engine_step"] = run_c5(torch, device, args)
         extra["c5_layer_decode"] = run_c5_layer(torch, device, stream)
         # BASELINE config 1 is a CPU config (fp32, which the GPU path does not
@@ -542,6 +543,62 @@ def run_c2_ctx1024(torch, device, stream, args):
     return {"workload": "BASELINE c2 at context 1024 (B8, 16q/2kv, D128, bs32, bf16)",
             "us_per_step": us, "tokens_per_s": C2["batch"] / (us * 1e-6),
             "algorithmic_bytes": nbytes, "hbm_gbs": gbs, "frac_of_peak": gbs / peak}
+
+
+def run_vllm_launcher(torch, device, stream, reps=200):
+    """The reference's own headline configuration (its only published
+    B8/ctx2048 number, benchmarks/results/vllm_qwen_attention_summary.md:24):
+    the vLLM decode launcher (flashdec/kernels/paged_decode.py:728-919) at B8,
+    context 2048, Qwen2.5-3B attention shape (16 q / 2 KV heads, head_dim
+    128), vLLM's 16-token NHD cache [blocks, 2, 16, kv_heads, 128] with the
+    fused current-token append (the step's K/V rows stored at slot_mapping
+    and attended), CUDA-graph replay over rotating pools larger than L2."""
+    from flashdec_b200.kernels.paged_decode import _vllm_paged_decode_attention_into
+    from oracle.paged_attention import attention_bytes
+
+    b, hq, hkv, d, bs, ctx = 8, 16, 2, 128, 16, 2048
+    nblk = ctx // bs
+    pool = 2 * b * nblk
+    g = torch.Generator(device=device).manual_seed(55)
+    pools = []
+    for _ in range(NUM_POOLS):
+        kv = torch.randn((pool, 2, bs, hkv, d), device=device, dtype=torch.bfloat16, generator=g)
+        bt = torch.randperm(pool, device=device, generator=g)[: b * nblk].reshape(b, nblk)
+        bt = bt.to(torch.int32).contiguous()
+        # the current token (position ctx - 1) goes to its page's last slot
+        slot = (bt[:, -1].to(torch.int64) * bs + (ctx - 1) % bs).contiguous()
+        q = torch.randn((b, hq, d), device=device, dtype=torch.bfloat16, generator=g)
+        k = torch.randn((b, hkv, d), device=device, dtype=torch.bfloat16, generator=g)
+        v = torch.randn((b, hkv, d), device=device, dtype=torch.bfloat16, generator=g)
+        pools.append((q, k, v, kv, bt, slot, torch.empty_like(q)))
+    sl = torch.full((b,), ctx, device=device, dtype=torch.int32)
+    # vLLM's split workspace (softmax_segm_*, 16 segments); the auto plan
+    # merges inside the kernel and does not touch it
+    acc = torch.empty((b, hq, 16, d), device=device, dtype=torch.float32)
+    mx = torch.empty((b, hq, 16), device=device, dtype=torch.float32)
+    sm = torch.empty((b, hq, 16), device=device, dtype=torch.float32)
+    state = {"i": 0}
+
+    def step():
+        q, k, v, kv, bt, slot, out = pools[state["i"] % len(pools)]
+        state["i"] += 1
+        _vllm_paged_decode_attention_into(q, k, v, kv, bt, sl, out, slot, acc, mx, sm,
+                                          num_reqs=b, num_q_heads=hq, num_kv_heads=hkv,
+                                          head_dim=d, block_size=bs, sm_scale=d ** -0.5,
+                                          num_splits=0)
+
+    us = _graph_time_us(torch, stream, step, reps=max(10, reps // 12), inner=NUM_POOLS * 10)
+    # K/V read once per KV head (the cache holds ctx - 1 tokens, the current
+    # one comes from the call), plus the appended rows read and stored
+    nbytes = attention_bytes([ctx] * b, hq, hkv, d, bs) + 2 * b * hkv * d * 2 * 2
+    peak, _ = _peaks()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": "vLLM launcher (reference headline config): B8 ctx2048, 16q/2kv, D128, "
+                        "16-token NHD 5-D cache, fused current-token append, graph replay",
+            "us_per_step": us, "tokens_per_s": b / (us * 1e-6), "algorithmic_bytes": nbytes,
+            "hbm_gbs": gbs, "frac_of_peak": gbs / peak,
+            "reference_published_us": 38.528,
+            "reference_published": "RTX 5070, benchmarks/results/vllm_qwen_attention_summary.md:24"}
 
 
 def run_c3(torch, device, stream, cpu_seconds=2.0, api_reps=200):
@@ -1032,10 +1089,11 @@ def main():
                     help="print decode latency over batch x context (Qwen shape), one JSON "
                          "line per point, and exit")
     ap.add_argument("--kernel-only", nargs="?", const="c2", default=None,
-                    choices=["c2", "c3", "c4", "c5"],
+                    choices=["c2", "c3", "c4", "c5", "vllm"],
                     help="time only one device-resident workload (no e2e or CPU legs): c2 "
                          "(default), c3 (fused RoPE + append), c4 (16 requests of the ragged "
-                         "batch, 1.5 GB of KV) or c5 (one layer of the c5 shape, plain decode); "
+                         "batch, 1.5 GB of KV), c5 (one layer of the c5 shape, plain decode) or "
+                         "vllm (the vLLM launcher at B8 ctx2048 with the fused append); "
                          "the small cases used for ncu captures")
     args = ap.parse_args()
 
@@ -1055,7 +1113,7 @@ def main():
         for point in run_sweep(torch, device, torch.cuda.Stream(device)):
             print(json.dumps({"sweep": "qwen-shape decode", **point}), flush=True)
         return
-    if args.kernel_only in ("c3", "c4", "c5"):
+    if args.kernel_only in ("c3", "c4", "c5", "vllm"):
         import torch
 
         device = torch.device("cuda", 0)
@@ -1065,6 +1123,8 @@ def main():
             res = run_c3(torch, device, stream, cpu_seconds=0.0, api_reps=0)
         elif args.kernel_only == "c5":
             res = run_c5_layer(torch, device, stream, reps=min(args.steps, 300))
+        elif args.kernel_only == "vllm":
+            res = run_vllm_launcher(torch, device, stream, reps=min(args.steps, 200))
         else:
             res = run_ragged(torch, None, device, 0, 1, stream, args, batch=16)
         print(json.dumps({"kernel_only": args.kernel_only, **res}), flush=True)

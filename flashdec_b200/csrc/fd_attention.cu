@@ -2697,6 +2697,7 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
     CUtensorMap wk = mk, wv = mv;
     bool wtma = true;
     w.num_kv_heads = a->num_kv_heads;
+    w.spec_skew = wave_spec_skew();
     if (D == 128 && a->block_size == 32) {
       // a contiguous token-major pair of caches: one box per page moves K and V
       CacheDesc cd;

@@ -57,12 +57,14 @@ constexpr int kWaveConsumerThreads = 32 * kWaveConsumerWarps;
 constexpr int kWaveTileBars = 32;    // tile i completes on full barrier i % 32
 constexpr int kWaveMaxStages = 16;
 constexpr int kWaveMiscInts = 16;    // [0] abort, [1] last ticket, [2] prefetch hint,
-                                     // [3] cluster merge arrived
+                                     // [3] cluster merge arrived, [4..5] appended slot,
+                                     // [6] speculative first page, [7] speculative length + 1,
+                                     // [8] speculative window ready
 constexpr int kWaveBarConsumers = 1;  // named barrier of the consumer warps
 constexpr int kWavePrefetchPages = 64;
 // barriers (full, empty, cluster merge), tile masks, misc
-constexpr int kWaveCtlBytes = (kWaveTileBars + kWaveMaxStages + 2) * 8 + kWaveTileBars * 4 +
-                              kWaveMiscInts * 4 + 2 * 64 * 4 + 2 * 128 * 2;
+constexpr int kWaveCtlBytes = (2 * kWaveTileBars + kWaveMaxStages + 2) * 8 + kWaveTileBars * 4 +
+                              kWaveMiscInts * 4 + 2 * 64 * 4 + 2 * 128 * 2 + 32 * 4;
 // Shared-memory budget that keeps two CTAs resident per SM (228 KB per SM,
 // 1 KB reserved per CTA).
 constexpr size_t kWaveSmemBudget = 112 * 1024;
@@ -148,13 +150,17 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(rbuf + p.recv_bytes);
   uint64_t* empty_bar = full_bar + kWaveTileBars;
   uint64_t* merge_bar = empty_bar + kWaveMaxStages;
-  uint32_t* tile_mask = reinterpret_cast<uint32_t*>(merge_bar + 2);
+  // "verified": tile i's pages are the ones the real block table names (the
+  // first group may be issued from the prefetch warp's speculative read)
+  uint64_t* ver_bar = merge_bar + 2;
+  uint32_t* tile_mask = reinterpret_cast<uint32_t*>(ver_bar + kWaveTileBars);
   int* misc = reinterpret_cast<int*>(tile_mask + kWaveTileBars);
   // fused append: the appended token's slot (misc[4..5]), the cos / sin of
   // its position per pair index, and its K (rotated) and V rows
   int64_t* app_slot = reinterpret_cast<int64_t*>(misc + 4);
   float* rope_tab = reinterpret_cast<float*>(misc + kWaveMiscInts);  // [2][64]
   T* app_row = reinterpret_cast<T*>(rope_tab + 2 * 64);              // [2][D]
+  int* spec_win = reinterpret_cast<int*>(app_row + 2 * 128);           // [32] speculative block ids
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -175,7 +181,10 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   // The next kernel of the stream may become resident now; it waits for
   // this one to finish before it reads anything this one writes.
   pdl_launch_dependents();
-  if (tid < kWaveTileBars) mbar_init(smem_u32(&full_bar[tid]), 1);
+  if (tid < kWaveTileBars) {
+    mbar_init(smem_u32(&full_bar[tid]), 1);
+    mbar_init(smem_u32(&ver_bar[tid]), 1);
+  }
   if (tid >= 32 && tid < 32 + NST) mbar_init(smem_u32(&empty_bar[tid - 32]), 1);
   if (kCluster && tid == 64) {
     // The peers' pushes land on this CTA's merge barrier as bytes (st.async);
@@ -211,7 +220,7 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     const int tiles = static_cast<int>((n + kTile - 1) / kTile);
     int t0, t1;
     wave_range(split, S, tiles, t0, t1);
-    const int64_t nlb = (n + bs - 1) >> bs_shift;
+    const int64_t nlb = ((kAppend && n > 0 ? n - 1 : n) + bs - 1) >> bs_shift;
     const int64_t pg0 = static_cast<int64_t>(t0) << ppt_shift;
     int64_t pg1 = min(static_cast<int64_t>(t1) << ppt_shift, nlb);
     pg1 = min(pg1, pg0 + kWavePrefetchPages);
@@ -226,6 +235,20 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       int64_t blk = -1;
       if (lb < pg1) blk = load_index_cg(p.bt, p.bt64, static_cast<int64_t>(b) * p.bts0 + lb * p.bts1);
       const int npg = static_cast<int>(min(static_cast<int64_t>(32), pg1 - lb0));
+      if (lb0 == pg0) {
+        // the first window, for the producer to issue from before its own
+        // (real) read of the block table returns
+        spec_win[lane] = (p.spec_skew && blk >= 0)
+                             ? static_cast<int>((blk + p.spec_skew) % p.num_blocks)
+                             : static_cast<int>(blk);
+        __syncwarp();
+        if (lane == 0) {
+          abort_flag[6] = static_cast<int>(pg0);
+          abort_flag[7] = static_cast<int>(n) + 1;
+          __threadfence_block();
+          abort_flag[8] = 1;
+        }
+      }
       for (int j = 0; j < npg; ++j) {
         const int64_t bj = __shfl_sync(0xffffffffu, blk, j);
         if (bj < 0 || bj >= p.num_blocks) continue;  // warp-uniform
@@ -293,6 +316,87 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     int64_t wb = static_cast<int64_t>(g0) << ppt_shift;
     int win = bt_entry(wb + lane);
     int win_next = bt_entry(wb + 32 + lane);
+    const int ppt = 1 << ppt_shift;
+    const uint32_t tile_bits = (1u << ppt) - 1u;
+    const uint32_t page_bytes = static_cast<uint32_t>(bs * D * 2 * 2);  // K and V of one page
+
+    // Issue the TMA boxes of tiles [i0, i0 + np / ppt): lane j's block id
+    // `blk` is page j of the group, `pages` the pages to load, each tile's
+    // bytes counted on bars[tile].  One box per (page, plane) -- a page's
+    // tokens x all of head_dim (the head_dim 128 map carries the 64-dim half
+    // axis), [half][tokens][64] in the stage -- or, with the K + V pair map,
+    // one box per page for both planes.  Every box of a group is issued by
+    // one warp instruction (lane = box): each TMA operation costs issue time
+    // on the SM, and an instruction issuing many costs far less per operation
+    // than one issuing a few.
+    auto issue = [&](int i0, int np, uint32_t pages, int blk, uint64_t* bars) {
+      if (D == 128 && kPageRows == 0 && p.kv_box) {
+        if (lane < np && ((pages >> lane) & 1u)) {
+          const int i = i0 + (lane >> ppt_shift);
+          tma_load_5d(smem_u32(stages + (i % NST) * SM::kStageBytes), &tmap_k,
+                      smem_u32(&bars[i % kWaveTileBars]), 0, 0, 0,
+                      blk * p.num_kv_heads + kv_head, 0, policy);
+        }
+        return;
+      }
+      const int nops = np * 2;
+      for (int base = 0; base < nops; base += 32) {
+        const int op = base + lane;
+        const int page = op >> 1;  // page of the group
+        const int pblk = __shfl_sync(0xffffffffu, blk, page & 31);
+        if (op < nops && ((pages >> page) & 1u)) {
+          const int plane = op & 1;  // 0: K, 1: V
+          const int i = i0 + (page >> ppt_shift);
+          const int j = page & (ppt - 1);  // page of the tile
+          const uint32_t sbase = smem_u32(stages + (i % NST) * SM::kStageBytes) +
+                                 plane * (SM::kHalves * SM::kHalfBytes);
+          const uint32_t fbar = smem_u32(&bars[i % kWaveTileBars]);
+          const int* perm = plane ? p.vperm : p.kperm;
+          const CUtensorMap* map = plane ? &tmap_v : &tmap_k;
+          if constexpr (D == 128) {
+            tma_load_5d(sbase + j * (bs * 256), map, fbar, 0, tmap_coord(perm[0], kv_head, pblk),
+                        tmap_coord(perm[1], kv_head, pblk), tmap_coord(perm[2], kv_head, pblk),
+                        tmap_coord(perm[3], kv_head, pblk), policy);
+          } else {
+            tma_load_4d(sbase + ((j * bs) << 7), map, fbar, 0, tmap_coord(perm[0], kv_head, pblk),
+                        tmap_coord(perm[1], kv_head, pblk), tmap_coord(perm[2], kv_head, pblk),
+                        policy);
+          }
+        }
+      }
+    };
+
+    // ---- speculative first group ----------------------------------------
+    // When the prefetch warp has published the block-table window it read
+    // before griddepcontrol.wait, the first group goes out from it now,
+    // while the real reads above are in flight.  Only the choice of pages is
+    // speculative: the bytes are read after the wait.  Below, each tile is
+    // checked against the real block table and either confirmed on its
+    // "verified" barrier or, once the speculative copy has landed, loaded
+    // again from the right pages onto that barrier.
+    int spec_ng = 0;          // tiles issued from the speculative window
+    uint32_t spec_pages = 0;  // bit j: page j of that group was loaded
+    int spec_blk = -1;        // lane j: its block id
+    if (abort_flag[8]) {
+      const int64_t ns = abort_flag[7] - 1;
+      int s0, s1;
+      wave_range(split, S, static_cast<int>((ns + kTile - 1) / kTile), s0, s1);
+      const int64_t nlb_s = ((kAppend && ns > 0 ? ns - 1 : ns) + bs - 1) >> bs_shift;
+      const int64_t pgs = static_cast<int64_t>(s0) << ppt_shift;
+      spec_ng = min(min(s1 - s0, NST), 32 >> ppt_shift);
+      const int nps = spec_ng << ppt_shift;
+      spec_blk = spec_win[lane];
+      const bool pv = lane < nps && (pgs + lane) < nlb_s && spec_blk >= 0 && spec_blk < p.num_blocks;
+      spec_pages = __ballot_sync(0xffffffffu, pv);
+      if (lane < spec_ng) {
+        const uint32_t tmask = (spec_pages >> (lane << ppt_shift)) & tile_bits;
+        tile_mask[lane] = tmask;
+        mbar_arrive_expect_tx(smem_u32(&full_bar[lane]), static_cast<uint32_t>(__popc(tmask)) * page_bytes);
+      }
+      __syncwarp();
+      issue(0, nps, spec_pages, spec_blk, full_bar);
+    }
+
     n = wave_clamp_len(p, __shfl_sync(0xffffffffu, n, 0));
     // reference MASK_INVALID_SLOT: a negative slot attends to nothing
     if (kAppend && __shfl_sync(0xffffffffu, slotv, 0) < 0) n = 0;
@@ -304,15 +408,59 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     const int64_t nlb = ((kAppend && n > 0 ? n - 1 : n) + bs - 1) >> bs_shift;
     const int ntile = t1 - t0;
     bool bad = false;
-    const int ppt = 1 << ppt_shift;
-    // Tiles go out in groups: lane l of the warp does the bookkeeping of
-    // tile i0 + l (its stage's "empty" wait, its page mask and the byte
-    // count on its "full" barrier), then every box of the group is issued by
-    // one warp instruction (lane = box).  Each TMA operation costs issue
-    // time on the SM, and a warp instruction issuing many of them costs far
-    // less per operation than one issuing a few.  The first group fills
-    // every stage; later groups take at most half the ring.
-    for (int i0 = 0; i0 < ntile;) {
+    bool alive = true;
+
+    // ---- check the speculative group against the real block table -------
+    int i_start = 0;
+    if (spec_ng > 0) {
+      const int nv = min(spec_ng, ntile);
+      const int64_t pg0 = static_cast<int64_t>(t0) << ppt_shift;
+      if (pg0 != wb) {
+        wb = pg0;
+        win = bt_entry(wb + lane);
+        win_next = bt_entry(wb + 32 + lane);
+      }
+      const int npv = nv << ppt_shift;
+      const int blk_r = win;  // lane j: page pg0 + j
+      const bool hr = lane < npv && (pg0 + lane) < nlb;
+      const bool pr = hr && blk_r >= 0 && blk_r < p.num_blocks;
+      bad = bad || (hr && !pr);
+      const uint32_t real_pages = __ballot_sync(0xffffffffu, pr);
+      const bool ps = (spec_pages >> lane) & 1u;
+      const bool same = lane >= npv || (pr == ps && (!pr || blk_r == spec_blk));
+      const uint32_t diff = __ballot_sync(0xffffffffu, !same);
+      const bool redo = lane < nv && ((diff >> (lane << ppt_shift)) & tile_bits) != 0;
+      const uint32_t redo_tiles = __ballot_sync(0xffffffffu, redo);
+      bool ok = true;
+      if (lane < nv) {
+        if (!redo) {
+          mbar_arrive(smem_u32(&ver_bar[lane]));
+        } else {
+          // the speculative copy lands before the right pages overwrite the stage
+          ok = mbar_wait(smem_u32(&full_bar[lane]), 0u, p.status, abort_flag);
+          if (ok) {
+            const uint32_t tmask = (real_pages >> (lane << ppt_shift)) & tile_bits;
+            tile_mask[lane] = tmask;
+            mbar_arrive_expect_tx(smem_u32(&ver_bar[lane]),
+                                  static_cast<uint32_t>(__popc(tmask)) * page_bytes);
+          }
+        }
+      }
+      alive = __all_sync(0xffffffffu, ok);
+      if (alive && redo_tiles) {
+        const uint32_t redo_pages =
+            __ballot_sync(0xffffffffu, pr && ((redo_tiles >> (lane >> ppt_shift)) & 1u));
+        issue(0, npv, redo_pages, blk_r, ver_bar);
+      }
+      i_start = nv;
+    }
+
+    // ---- the remaining tiles, in groups ---------------------------------
+    // Lane l of the warp does the bookkeeping of tile i0 + l (its stage's
+    // "empty" wait, its page mask, the byte count on its "full" barrier and
+    // the arrival on its "verified" one).  The first group fills every free
+    // stage; later groups take at most half the ring.
+    for (int i0 = i_start; alive && i0 < ntile;) {
       const int64_t pg0 = static_cast<int64_t>(t0 + i0) << ppt_shift;
       if (pg0 < wb || pg0 >= wb + 64) {
         wb = pg0;  // (re)load the window at this group
@@ -340,54 +488,21 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
                          p.status, abort_flag);
         }
         if (ok) {
-          const uint32_t tmask = (pages >> (lane << ppt_shift)) & ((1u << ppt) - 1u);
+          const uint32_t tmask = (pages >> (lane << ppt_shift)) & tile_bits;
           tile_mask[i % kWaveTileBars] = tmask;
           mbar_arrive_expect_tx(smem_u32(&full_bar[i % kWaveTileBars]),
-                                static_cast<uint32_t>(__popc(tmask)) * (bs * D * 2 * 2));
+                                static_cast<uint32_t>(__popc(tmask)) * page_bytes);
+          mbar_arrive(smem_u32(&ver_bar[i % kWaveTileBars]));
         }
       }
       if (!__all_sync(0xffffffffu, ok)) break;
-      // one box per (page, plane): a page's tokens x all of head_dim (the
-      // head_dim 128 map carries the 64-dim half axis), [half][tokens][64]
-      // in the stage; with the K + V pair map one box per page moves both
-      // planes
-      if (D == 128 && kPageRows == 0 && p.kv_box) {
-        const int pblk = blk_l;  // lane = page of the group
-        if (lane < np && ((pages >> lane) & 1u)) {
-          const int i = i0 + (lane >> ppt_shift);
-          tma_load_5d(smem_u32(stages + (i % NST) * SM::kStageBytes), &tmap_k,
-                      smem_u32(&full_bar[i % kWaveTileBars]), 0, 0, 0,
-                      pblk * p.num_kv_heads + kv_head, 0, policy);
-        }
-        i0 += ng;
-        continue;
-      }
-      const int nops = np * 2;
-      for (int base = 0; base < nops; base += 32) {
-        const int op = base + lane;
-        const int page = op >> 1;  // page of the group
-        const int pblk = __shfl_sync(0xffffffffu, blk_l, page & 31);
-        if (op < nops && ((pages >> page) & 1u)) {
-          const int plane = op & 1;  // 0: K, 1: V
-          const int i = i0 + (page >> ppt_shift);
-          const int j = page & (ppt - 1);  // page of the tile
-          const uint32_t sbase = smem_u32(stages + (i % NST) * SM::kStageBytes) +
-                                 plane * (SM::kHalves * SM::kHalfBytes);
-          const uint32_t fbar = smem_u32(&full_bar[i % kWaveTileBars]);
-          const int* perm = plane ? p.vperm : p.kperm;
-          const CUtensorMap* map = plane ? &tmap_v : &tmap_k;
-          if constexpr (D == 128) {
-            tma_load_5d(sbase + j * (bs * 256), map, fbar, 0, tmap_coord(perm[0], kv_head, pblk),
-                        tmap_coord(perm[1], kv_head, pblk), tmap_coord(perm[2], kv_head, pblk),
-                        tmap_coord(perm[3], kv_head, pblk), policy);
-          } else {
-            tma_load_4d(sbase + ((j * bs) << 7), map, fbar, 0, tmap_coord(perm[0], kv_head, pblk),
-                        tmap_coord(perm[1], kv_head, pblk), tmap_coord(perm[2], kv_head, pblk),
-                        policy);
-          }
-        }
-      }
+      issue(i0, np, pages, blk_l, full_bar);
       i0 += ng;
+    }
+    // speculative tiles this CTA turned out not to need still land in its
+    // shared memory: the CTA waits for them before it may exit
+    if (lane < spec_ng && lane >= ntile) {
+      mbar_wait(smem_u32(&full_bar[lane]), 0u, p.status, abort_flag);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, FD_STATUS_BAD_BLOCK_ID);
     return;
@@ -517,8 +632,12 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
   for (int i = warp; i < ntile; i += kWaveConsumerWarps) {
     const int t = t0 + i;
     const int stage = i % NST;
-    if (!mbar_wait(smem_u32(&full_bar[i % kWaveTileBars]),
-                   static_cast<uint32_t>(i / kWaveTileBars) & 1u, p.status, abort_flag)) {
+    // the tile's bytes have landed, and its pages are the block table's
+    // (a speculatively chosen page that turned out wrong is loaded again and
+    // lands on the "verified" barrier)
+    const uint32_t par = static_cast<uint32_t>(i / kWaveTileBars) & 1u;
+    if (!mbar_wait(smem_u32(&full_bar[i % kWaveTileBars]), par, p.status, abort_flag) ||
+        !mbar_wait(smem_u32(&ver_bar[i % kWaveTileBars]), par, p.status, abort_flag)) {
       continue;
     }
     uint8_t* sb = stages + stage * SM::kStageBytes;
@@ -1096,6 +1215,14 @@ int wave_layout(const WaveParams& p, const CUtensorMap& mk, const CUtensorMap& m
 }
 
 }  // namespace
+
+int wave_spec_skew() {
+  static const int skew = [] {
+    const char* v = std::getenv("FLASHDEC_B200_TEST_SPEC_SKEW");
+    return v ? std::atoi(v) : 0;
+  }();
+  return skew;
+}
 
 bool wave_enabled() {
   static const bool on = [] {

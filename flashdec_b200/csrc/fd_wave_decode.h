@@ -29,6 +29,10 @@ struct WaveParams {
   // kv_box: the K map is a K + V pair map (get_kv_pair_tensor_map) and one
   // box moves a page's K and V; v_first: V's plane comes first in the stage
   int kv_box, v_first, num_kv_heads;
+  // test hook: added to every speculatively read block id (mod num_blocks)
+  // so that the check of the speculative first group must re-load it
+  // (FLASHDEC_B200_TEST_SPEC_SKEW; 0 in normal use)
+  int spec_skew;
   // the caches (unit dim stride) for the L2 prefetch of the next call's pages
   const void* k;
   int64_t ks0, ks1, ks2;
@@ -71,6 +75,9 @@ struct WaveParams {
   int rope_pos64;
   int64_t rope_pos_stride;
 };
+
+// FLASHDEC_B200_TEST_SPEC_SKEW (read once; 0 when unset).
+int wave_spec_skew();
 
 // Whether fd_paged_decode may use the one-wave kernel for small batches
 // (default on; FLASHDEC_B200_WAVE=0 keeps the older split schedule).

@@ -1,9 +1,10 @@
 """Generate the golden fixtures by running the REFERENCE implementation.
 
-Run from the repository root in a container that has a checkout of
-cysong2025/flashdec (``FLASHDEC_REF``, default ``/root/reference``):
+Run from the repository root with ``FLASHDEC_REF`` naming a checkout of
+cysong2025/flashdec (or a directory the reference is installed into, such as
+``baseline/_ref``):
 
-    python tests/golden/make_golden.py
+    FLASHDEC_REF=<path to the reference> python tests/golden/make_golden.py
 
 It imports the reference's own oracles -- ``flashdec.paged_reference``,
 ``flashdec.rope``, ``flashdec.cache.PagedKVCache`` and
@@ -37,7 +38,6 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
 sys.path.insert(0, str(REPO))
-sys.path.insert(0, os.environ.get("FLASHDEC_REF", "/root/reference"))
 
 import torch  # noqa: E402
 
@@ -243,6 +243,11 @@ def split_policy_fixture():
 
 
 def main():
+    # the reference is imported lazily by each fixture function; importing
+    # this module (for LEDGER_METRICS) needs no reference
+    if not os.environ.get("FLASHDEC_REF"):
+        sys.exit("set FLASHDEC_REF to a checkout (or install) of the reference, cysong2025/flashdec")
+    sys.path.insert(0, os.environ["FLASHDEC_REF"])
     np.savez_compressed(HERE / "attn_golden.npz", **attention_fixtures())
     np.savez_compressed(HERE / "rope_golden.npz", **rope_fixtures())
     (HERE / "ledger_golden.json").write_text(json.dumps(ledger_fixture(), indent=0))

@@ -38,6 +38,13 @@ def main(backend: str, out_path: str) -> None:
     prompts = [TokensPrompt(prompt_token_ids=[int(x) for x in rng.integers(3, 1000, size=n)])
                for n in lengths]
     params = SamplingParams(max_tokens=12, temperature=0.0, logprobs=3, detokenize=False)
+    # set only by flashdec_b200.vllm_plugin.register(), which vLLM's own
+    # general-plugin loader calls through the installed entry point
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum
+    try:
+        custom_path = AttentionBackendEnum.CUSTOM.get_path()
+    except ValueError:
+        custom_path = ""
     out = []
     for o in llm.generate(prompts, params):
         c = o.outputs[0]
@@ -45,7 +52,8 @@ def main(backend: str, out_path: str) -> None:
                     "logprobs": [{str(k): float(v.logprob) for k, v in d.items()}
                                  for d in (c.logprobs or [])]})
     with open(out_path, "w") as f:
-        json.dump({"backend": backend, "flashdec_launches": calls["n"], "outputs": out}, f)
+        json.dump({"backend": backend, "flashdec_launches": calls["n"], "outputs": out,
+                   "plugin_loaded": custom_path.startswith("flashdec_b200.")}, f)
 
 
 if __name__ == "__main__":
