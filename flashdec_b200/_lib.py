@@ -102,6 +102,7 @@ EXPORTED_SYMBOLS = (
 
 _lock = threading.Lock()
 _lib = None
+_hostpath = None
 
 
 class FlashDecNativeError(RuntimeError):
@@ -151,6 +152,32 @@ def load_library():
             getattr(lib, name).restype = ctypes.c_int
         _lib = lib
         return lib
+
+
+def load_hostpath():
+    """Import (once) the C++ host-path module ``_hostpath`` and point it at
+    this process's library entry points.  It is built in-tree beside the
+    library; a missing module raises like a missing library."""
+    global _hostpath
+    if _hostpath is not None:
+        return _hostpath
+    lib = load_library()
+    with _lock:
+        if _hostpath is not None:
+            return _hostpath
+        try:
+            from . import _hostpath as hp
+        except ImportError as exc:
+            raise RuntimeError(
+                f"flashdec_b200._hostpath is missing or does not load ({exc}): build it with "
+                "`python -m flashdec_b200.build`") from exc
+        if hp.ARGS_BYTES != ctypes.sizeof(PagedDecodeArgs):
+            raise RuntimeError("flashdec_b200._hostpath was built against another "
+                               "fd_paged_decode_args layout: rebuild it")
+        hp.set_entry_points(ctypes.cast(lib.fd_paged_decode, ctypes.c_void_p).value,
+                            ctypes.cast(lib.fd_cascade_decode, ctypes.c_void_p).value)
+        _hostpath = hp
+        return hp
 
 
 def check(rc: int, what: str) -> None:

@@ -1,8 +1,10 @@
-"""Build libflashdec_b200.so (the C-ABI + sm_100a kernels) in-tree with nvcc.
+"""Build libflashdec_b200.so (the C-ABI + sm_100a kernels) in-tree with nvcc,
+and the C++ host-path module ``_hostpath`` (csrc/fd_hostpath.cpp) with g++
+against the installed torch.
 
     python -m flashdec_b200.build          # or: python flashdec_b200/build.py
 
-The library lands next to this file so that it travels with the source tree.
+Both land next to this file so that they travel with the source tree.
 Objects are compiled in parallel and re-used when their sources are older.
 """
 
@@ -13,6 +15,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -60,8 +63,49 @@ def _compile(src: str, verbose: bool) -> Path:
     return obj
 
 
+HOSTPATH_SRC = CSRC / "fd_hostpath.cpp"
+HOSTPATH = PKG / ("_hostpath" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_hostpath(verbose: bool = False, force: bool = False) -> Path:
+    """Compile the torch extension module of the C++ host path with g++
+    (no JIT: the module is a plain in-tree file, loaded like the library)."""
+    import torch
+    from torch.utils import cpp_extension
+
+    newest = max(HOSTPATH_SRC.stat().st_mtime, (INCLUDE / "flashdec_b200.h").stat().st_mtime)
+    if HOSTPATH.exists() and HOSTPATH.stat().st_mtime >= newest and not force:
+        return HOSTPATH
+    incs = cpp_extension.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"],
+                                                              str(INCLUDE)]
+    libs = cpp_extension.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = HOSTPATH.with_suffix(".tmp")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_hostpath",
+           "-DTORCH_API_INCLUDE_EXTENSION_H", *[f"-I{d}" for d in incs],
+           str(HOSTPATH_SRC), "-o", str(tmp), *[f"-L{d}" for d in libs],
+           "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python", "-lcudart",
+           *[f"-Wl,-rpath,{d}" for d in libs]]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed for {HOSTPATH_SRC.name}:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, HOSTPATH)
+    return HOSTPATH
+
+
 def build(verbose: bool = False, force: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
+    with concurrent.futures.ThreadPoolExecutor(max_workers=1) as hp:
+        hostpath = hp.submit(build_hostpath, verbose, force)
+        lib = _build_library(verbose, force)
+        hostpath.result()
+    return lib
+
+
+def _build_library(verbose: bool, force: bool) -> Path:
     if force:
         for o in BUILD.glob("*.o"):
             o.unlink()

@@ -267,6 +267,11 @@ class _FusedLayerLauncher:
             if s is not None:
                 da.scratch, da.scratch_bytes = s.data_ptr(), s.numel() * 4
         self.da = da
+        # the C++ host path runs each layer on these structs (kept alive here)
+        self.hostpath = _lib.load_hostpath()
+        self.da_addr = ctypes.addressof(da)
+        self.cascade_addr = (ctypes.addressof(self.cascade.args)
+                             if self.cascade is not None else 0)
 
     def _set_rope(self, rotary_dim, base):
         key = (rotary_dim, base)
@@ -277,28 +282,19 @@ class _FusedLayerLauncher:
             self.rope_key = key
 
     def run(self, layer_idx, q, k, v, rotary_dim, base):
-        """RoPE + K/V store + decode in one launch; returns the output."""
-        if tuple(q.shape) != self.qshape or not q.is_contiguous():
-            raise ValueError("q must be a contiguous [num_requests, num_q_heads, head_dim] tensor "
-                             "matching the transaction")
-        if tuple(k.shape) != self.kvshape or tuple(v.shape) != self.kvshape or \
-                not k.is_contiguous() or not v.is_contiguous():
-            raise ValueError("k and v must be contiguous [num_requests, num_kv_heads, head_dim] "
-                             "tensors matching the transaction")
-        self._set_rope(rotary_dim, base)
-        out = torch.empty(self.qshape, dtype=q.dtype, device=q.device)
-        da = self.da
-        da.q, da.out, da.append_k, da.append_v = (q.data_ptr(), out.data_ptr(), k.data_ptr(),
-                                                  v.data_ptr())
-        da.k_cache = self.k_base + layer_idx * self.k_layer_bytes
-        da.v_cache = self.v_base + layer_idx * self.v_layer_bytes
-        stream = ctypes.c_void_p(_native.stream_handle(self.device))
-        if self.cascade is not None:
-            self.check(self.lib.fd_cascade_decode(ctypes.byref(da),
-                                                  ctypes.byref(self.cascade.args), stream),
-                       "fd_cascade_decode")
-        else:
-            self.check(self.lib.fd_paged_decode(ctypes.byref(da), stream), "fd_paged_decode")
+        """RoPE + K/V store + decode in one launch; returns the output.
+
+        The C++ host path checks that q, k and v are contiguous and match
+        the transaction's shapes (ValueError otherwise), allocates the
+        output, sets the layer's pointers and launches on the current
+        stream."""
+        if (rotary_dim, base) != self.rope_key:
+            self._set_rope(rotary_dim, base)
+        out = self.hostpath.layer_run(self.da_addr, self.cascade_addr, q, k, v,
+                                      self.k_base + layer_idx * self.k_layer_bytes,
+                                      self.v_base + layer_idx * self.v_layer_bytes)
+        if type(out) is int:
+            self.check(out, "fd_cascade_decode" if self.cascade_addr else "fd_paged_decode")
         return out
 
 

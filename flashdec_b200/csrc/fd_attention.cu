@@ -2233,6 +2233,8 @@ int validate(const fd_paged_decode_args* a) {
 //     schedule over the whole batch.
 constexpr int kSplitMaxTilesPerCta = 32;
 constexpr int kSplitMinTilesPerCta = 2;
+constexpr int kWaveSplitCap = 14;
+constexpr int kWaveLongTiles = 12;
 
 struct Plan {
   int splits;    // 0: length-balanced persistent schedule
@@ -2256,6 +2258,16 @@ Plan make_plan(const fd_paged_decode_args& a, const Derived& dv, const DeviceInf
   if (a.max_ctas <= 0 && pairs <= nsm && pairs * pl.cap_tiles <= nsm * kSplitMaxTilesPerCta) {
     int64_t s = nsm / pairs;
     s = std::min<int64_t>(s, std::max(1, pl.cap_tiles / kSplitMinTilesPerCta));
+    if (wave_enabled() && a.epilogue == FD_EPILOGUE_FUSED) {
+      // One-wave kernel (two CTAs fit an SM): clusters above 14 CTAs cost
+      // more in residency than they add; once a split would hold 12 tiles or
+      // more, about 1.3 CTAs per SM beat one (measured over B1-B16,
+      // contexts 1k-8k).
+      s = std::min<int64_t>(s, kWaveSplitCap);
+      if (pl.cap_tiles >= kWaveLongTiles * s)
+        s = std::max<int64_t>(s, std::min<int64_t>(kWaveSplitCap, nsm * 13 / 10 / pairs));
+      if (wave_splits_override() > 0) s = wave_splits_override();
+    }
     pl.splits = static_cast<int>(std::max<int64_t>(1, s));
     pl.balanced = 1;
     pl.grid = static_cast<int>(pairs * pl.splits);

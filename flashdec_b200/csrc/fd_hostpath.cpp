@@ -1,0 +1,200 @@
+// Native host path of the Python API (module flashdec_b200._hostpath).
+//
+// The C-ABI launch of fd_paged_decode costs about as much host time as the
+// kernel launch itself; what a Python call adds on top (a signature of six
+// tensors, ctypes marshalling, the current-stream lookup) is larger than
+// that.  This module does the repeated part of two calls in C++ and leaves
+// everything else -- the first call of a signature, every check and error
+// message, workspace allocation -- to the Python code:
+//
+//  * decode_into(q, k, v, block_tables, seq_lens, out): the prepared call of
+//    paged_decode_attention_into with default scalar arguments.  A table maps
+//    (shape, stride, dtype, device of all six tensors, current stream) to an
+//    fd_paged_decode_args struct that the Python path prepared, checked and
+//    bound to that stream's workspace (register_decode copies it); a hit only
+//    sets the six data pointers and calls fd_paged_decode.  Returns 0, a
+//    negative FD_ERR_* code, or kMiss (Python then takes its own path).
+//
+//  * layer_run(args, cascade, q, k, v, k_layer, v_layer): one engine layer
+//    (fused RoPE + K/V store + decode) on a transaction's prepared struct:
+//    shape checks, the output allocation and one fd_paged_decode (or
+//    fd_cascade_decode) on the current stream.
+//
+// The entry points are taken as addresses from the already-loaded
+// libflashdec_b200.so (set_entry_points), so both paths call the same
+// library.  Every function runs with the GIL held, which serialises the
+// table and the structs it hands to the library.
+#include <torch/extension.h>
+
+#include <c10/cuda/CUDAFunctions.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <array>
+#include <cstdint>
+#include <cstring>
+#include <unordered_map>
+
+#include "flashdec_b200.h"
+
+namespace {
+
+using DecodeFn = int (*)(const fd_paged_decode_args*, void*);
+using CascadeFn = int (*)(const fd_paged_decode_args*, const fd_cascade_args*, void*);
+
+DecodeFn g_decode = nullptr;
+CascadeFn g_cascade = nullptr;
+
+constexpr int kMiss = 1;
+constexpr int kTensors = 6;
+constexpr int kMaxRank = 4;
+constexpr int kPerTensor = 2 + 2 * kMaxRank;  // rank | dtype+device, sizes, strides
+constexpr size_t kTableLimit = 256;
+
+struct Signature {
+  std::array<int64_t, kTensors * kPerTensor + 1> v{};
+  bool operator==(const Signature& o) const { return v == o.v; }
+};
+
+struct SignatureHash {
+  size_t operator()(const Signature& s) const {
+    uint64_t h = 1469598103934665603ull;
+    for (int64_t x : s.v) {
+      h ^= static_cast<uint64_t>(x) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    }
+    return static_cast<size_t>(h);
+  }
+};
+
+std::unordered_map<Signature, fd_paged_decode_args, SignatureHash> g_table;
+
+// false for a tensor the fast path does not describe (rank above four, not
+// on a CUDA device); the caller then takes the Python path
+bool signature(const at::Tensor* const* ts, cudaStream_t stream, Signature* s) {
+  int j = 0;
+  for (int i = 0; i < kTensors; ++i) {
+    const at::Tensor& t = *ts[i];
+    const int64_t r = t.dim();
+    if (r > kMaxRank || !t.is_cuda()) return false;
+    s->v[j++] = r;
+    s->v[j++] = static_cast<int64_t>(t.scalar_type()) * 1024 + t.get_device();
+    const auto sz = t.sizes();
+    const auto st = t.strides();
+    for (int64_t d = 0; d < kMaxRank; ++d) {
+      s->v[j++] = d < r ? sz[d] : 0;
+      s->v[j++] = d < r ? st[d] : 0;
+    }
+  }
+  s->v[j] = reinterpret_cast<int64_t>(stream);
+  return true;
+}
+
+void set_entry_points(int64_t decode, int64_t cascade) {
+  g_decode = reinterpret_cast<DecodeFn>(decode);
+  g_cascade = reinterpret_cast<CascadeFn>(cascade);
+}
+
+// Current stream of q's device, or nullptr when q's device is not the
+// current device (the Python path switches devices itself).
+bool current_stream_of(const at::Tensor& q, cudaStream_t* stream) {
+  const int dev = q.get_device();
+  if (dev < 0 || c10::cuda::current_device() != dev) return false;
+  *stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  return true;
+}
+
+int decode_into(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                const at::Tensor& out) {
+  if (!g_decode || g_table.empty()) return kMiss;
+  cudaStream_t stream;
+  if (!current_stream_of(q, &stream)) return kMiss;
+  const at::Tensor* ts[kTensors] = {&q, &k, &v, &block_tables, &seq_lens, &out};
+  Signature s;
+  if (!signature(ts, stream, &s)) return kMiss;
+  auto it = g_table.find(s);
+  if (it == g_table.end()) return kMiss;
+  fd_paged_decode_args& a = it->second;
+  a.q = q.data_ptr();
+  a.k_cache = k.data_ptr();
+  a.v_cache = v.data_ptr();
+  a.block_tables = block_tables.data_ptr();
+  a.seq_lens = seq_lens.data_ptr();
+  a.out = out.data_ptr();
+  return g_decode(&a, stream);
+}
+
+// Copies the struct at `args` (prepared and bound to the current stream's
+// workspace by the caller, who keeps that workspace alive for as long as the
+// entry exists) under the signature of these tensors on the current stream.
+bool register_decode(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                     const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                     const at::Tensor& out, int64_t args) {
+  cudaStream_t stream;
+  if (!current_stream_of(q, &stream)) return false;
+  const at::Tensor* ts[kTensors] = {&q, &k, &v, &block_tables, &seq_lens, &out};
+  Signature s;
+  if (!signature(ts, stream, &s)) return false;
+  if (g_table.size() >= kTableLimit) g_table.clear();
+  fd_paged_decode_args copy;
+  std::memcpy(&copy, reinterpret_cast<const void*>(args), sizeof(copy));
+  g_table[s] = copy;
+  return true;
+}
+
+void clear() { g_table.clear(); }
+
+int64_t table_size() { return static_cast<int64_t>(g_table.size()); }
+
+bool contiguous_shape(const at::Tensor& t, int64_t d0, int64_t d1, int64_t d2) {
+  if (t.dim() != 3 || !t.is_contiguous()) return false;
+  const auto s = t.sizes();
+  return s[0] == d0 && s[1] == d1 && s[2] == d2;
+}
+
+// One engine layer on the transaction's struct at `args` (and cascade
+// description at `cascade`, 0: none).  Returns the output tensor, or the
+// non-zero status of the library call as an int.
+py::object layer_run(int64_t args, int64_t cascade, const at::Tensor& q, const at::Tensor& k,
+                     const at::Tensor& v, int64_t k_layer, int64_t v_layer) {
+  auto* a = reinterpret_cast<fd_paged_decode_args*>(args);
+  if (!contiguous_shape(q, a->num_seqs, a->num_q_heads, a->head_dim)) {
+    throw py::value_error(
+        "q must be a contiguous [num_requests, num_q_heads, head_dim] tensor matching the "
+        "transaction");
+  }
+  if (!contiguous_shape(k, a->num_seqs, a->num_kv_heads, a->head_dim) ||
+      !contiguous_shape(v, a->num_seqs, a->num_kv_heads, a->head_dim)) {
+    throw py::value_error(
+        "k and v must be contiguous [num_requests, num_kv_heads, head_dim] tensors matching "
+        "the transaction");
+  }
+  cudaStream_t stream;
+  if (!current_stream_of(q, &stream)) {
+    throw py::value_error("q must be on the current CUDA device");
+  }
+  at::Tensor out = at::empty(q.sizes(), q.options());
+  a->q = q.data_ptr();
+  a->out = out.data_ptr();
+  a->append_k = k.data_ptr();
+  a->append_v = v.data_ptr();
+  a->k_cache = reinterpret_cast<void*>(k_layer);
+  a->v_cache = reinterpret_cast<void*>(v_layer);
+  const int rc = cascade ? g_cascade(a, reinterpret_cast<const fd_cascade_args*>(cascade), stream)
+                         : g_decode(a, stream);
+  if (rc != FD_OK) return py::int_(rc);
+  return py::cast(out);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "C++ host path of the prepared flashdec_b200 launches";
+  m.attr("MISS") = kMiss;
+  m.attr("ARGS_BYTES") = static_cast<int64_t>(sizeof(fd_paged_decode_args));
+  m.def("set_entry_points", &set_entry_points);
+  m.def("decode_into", &decode_into);
+  m.def("register_decode", &register_decode);
+  m.def("clear", &clear);
+  m.def("table_size", &table_size);
+  m.def("layer_run", &layer_run);
+}

@@ -1224,6 +1224,15 @@ int wave_spec_skew() {
   return skew;
 }
 
+int wave_splits_override() {
+  static const int s = [] {
+    const char* v = std::getenv("FLASHDEC_B200_WAVE_SPLITS");
+    const int n = v ? std::atoi(v) : 0;
+    return n >= 1 && n <= kWaveMaxSplits ? n : 0;
+  }();
+  return s;
+}
+
 bool wave_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("FLASHDEC_B200_WAVE");

@@ -82,6 +82,9 @@ int wave_spec_skew();
 // Whether fd_paged_decode may use the one-wave kernel for small batches
 // (default on; FLASHDEC_B200_WAVE=0 keeps the older split schedule).
 bool wave_enabled();
+// FLASHDEC_B200_WAVE_SPLITS=S (1..16): split count of the length-balanced
+// small-batch plan, for tuning sweeps (0: the built-in rule)
+int wave_splits_override();
 
 // Launch the one-wave kernel over grid (splits, head blocks, sequences),
 // splits <= kWaveMaxSplits.  The tensor maps move one page plane per box:

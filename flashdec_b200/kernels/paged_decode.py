@@ -22,6 +22,7 @@ reference's tests use):
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -62,6 +63,15 @@ def _launch_prepared(prep, q, k_cache, v_cache, block_tables, seq_lens, out):
         with torch.cuda.device(dev):
             prep.launch(q, k_cache, v_cache, block_tables, seq_lens, out,
                         _native.stream_handle(dev))
+
+
+def _register(prep, q, k_cache, v_cache, block_tables, seq_lens, out):
+    """Hand the struct that just launched (bound to the current stream's
+    workspace, which ``prep`` keeps alive while it is in ``_PREPARED``) to
+    the C++ host path under this call's signature."""
+    with prep.lock:
+        _lib.load_hostpath().register_decode(q, k_cache, v_cache, block_tables, seq_lens, out,
+                                             ctypes.addressof(prep.args))
 
 
 def _layout_axes(kv_layout):
@@ -220,6 +230,23 @@ def paged_decode_attention_into(
     attention launch; rows with ``slot_mapping < 0`` get a zero output and no
     store.
     """
+    # The call with every scalar at its default goes to the C++ host path
+    # first: a signature it has seen on this stream launches there.
+    default_call = (sm_scale is None and block_size is None and num_stages is None
+                    and split_kv_workspace is None and append_k is None and append_v is None
+                    and slot_mapping is None and type(num_warps) is int and num_warps == 2
+                    and type(num_splits) is int and num_splits == 1
+                    and kv_layout == "token_major")
+    if default_call:
+        hp = _lib.load_hostpath()
+        try:
+            rc = hp.decode_into(q, k_cache, v_cache, block_tables, seq_lens, out)
+        except TypeError:  # not tensors: the checks below raise the reference's errors
+            rc = hp.MISS
+        if rc == 0:
+            return out
+        if rc < 0:
+            _lib.check(rc, "fd_paged_decode")
     key = None
     if (split_kv_workspace is None and type(num_splits) is int and num_splits == 1
             and append_k is None and append_v is None and slot_mapping is None):
@@ -233,6 +260,8 @@ def paged_decode_attention_into(
             prep = _PREPARED.get(key)
             if prep is not None:
                 _launch_prepared(prep, q, k_cache, v_cache, block_tables, seq_lens, out)
+                if default_call:
+                    _register(prep, q, k_cache, v_cache, block_tables, seq_lens, out)
                 return out
 
     token_axis, _ = _layout_axes(kv_layout)
@@ -324,9 +353,12 @@ def paged_decode_attention_into(
                 block_size=block_size, num_seqs=num_seqs, num_splits=0)
             if len(_PREPARED) >= _PREPARED_LIMIT:
                 _PREPARED.clear()
+                _lib.load_hostpath().clear()  # its entries use the dropped workspaces
             _PREPARED[key] = prep
             prep.launch(q, k_cache, v_cache, block_tables, seq_lens, out,
                         _native.stream_handle(q.device))
+            if default_call:
+                _register(prep, q, k_cache, v_cache, block_tables, seq_lens, out)
             return out
         _native.paged_decode(
             q, k4, v4, block_tables, seq_lens, out, sm_scale=sm_scale,

@@ -376,3 +376,50 @@ def test_prepared_signature_reuses_checks_but_reads_new_data():
                                        to_dev(c1["v_cache"], c1["dtype"]),
                                        to_dev(c1["block_tables"]), to_dev(c1["seq_lens"]), out,
                                        num_splits=True)
+
+
+def test_cpp_host_path_hits_match_python_path_and_follow_streams():
+    """The C++ host path (flashdec_b200._hostpath) launches a default-argument
+    call whose signature the Python path prepared on the same stream: its
+    output is bit-identical to the Python path's, a new stream or a new shape
+    goes through the Python path first (and is then registered), and a
+    changed shape still gets the reference's errors."""
+    from flashdec_b200 import _lib
+    from flashdec_b200.kernels import paged_decode as pd
+
+    hp = _lib.load_hostpath()
+    c = cases.make_attn_case("split_257_193")
+    q = to_dev(c["q"], c["dtype"])
+    k, v = to_dev(c["k_cache"], c["dtype"]), to_dev(c["v_cache"], c["dtype"])
+    bt, sl = to_dev(c["block_tables"]), to_dev(c["seq_lens"])
+    pd._PREPARED.clear()
+    hp.clear()
+    ref = torch.empty_like(q)
+    pd.paged_decode_attention_into(q, k, v, bt, sl, ref)  # Python path: prepares, registers
+    assert hp.table_size() == 1
+    assert hp.decode_into(q, k, v, bt, sl, torch.empty_like(q)) == 0
+    fast = torch.empty_like(q)
+    pd.paged_decode_attention_into(q, k, v, bt, sl, fast)
+    torch.cuda.synchronize()
+    assert torch.equal(fast, ref)
+    # another stream: a miss, then the Python path binds that stream's workspace
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        assert hp.decode_into(q, k, v, bt, sl, fast) == hp.MISS
+        out2 = torch.empty_like(q)
+        pd.paged_decode_attention_into(q, k, v, bt, sl, out2)
+        assert hp.table_size() == 2
+        out3 = torch.empty_like(q)
+        pd.paged_decode_attention_into(q, k, v, bt, sl, out3)
+    side.synchronize()
+    assert torch.equal(out2, ref) and torch.equal(out3, ref)
+    # a different shape is not a hit and is checked by the Python path
+    with pytest.raises(ValueError, match="out must have the same shape as q"):
+        pd.paged_decode_attention_into(q, k, v, bt, sl, torch.empty_like(q[:1]))
+    # non-tensor arguments fall through to the reference's checks, which
+    # fail on them the way the reference's do (attribute access on a list)
+    with pytest.raises(AttributeError):
+        pd.paged_decode_attention_into(q, k, v, bt.tolist(), sl, fast)
+    want = paged_decode_attention_ref(c["q"], c["k_cache"], c["v_cache"], c["block_tables"],
+                                      c["seq_lens"])
+    assert_attention_close(to_np(fast), want)

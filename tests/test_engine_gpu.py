@@ -402,3 +402,46 @@ def test_cache_replays_reference_ledger_trace_with_data(golden_dir):
         if step == 24:
             cache.finish_request(active()[0])
     assert cache.validate_invariants()
+
+
+def test_fused_layer_shape_errors_abort_the_token():
+    """The fused layer launch (C++ host path) rejects a non-contiguous q and
+    k/v of the wrong shape with the engine's ValueError; the open token is
+    aborted, committed lengths are unchanged and the next token runs."""
+    from flashdec_b200 import DecodeEngine, PagedKVCache
+
+    L, hq, hkv, d = 2, 8, 2, 128
+    cache = PagedKVCache(L, hkv, d, 16, max_blocks=16, dtype=torch.bfloat16, device="cuda")
+    eng = DecodeEngine(cache, append_backend="fused_cuda")
+    ids = ["a", "b"]
+    for r in ids:
+        eng.add_request(r)
+    eng.admit()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn((2, hq, d), device="cuda", dtype=torch.bfloat16, generator=g)
+    k = torch.randn((2, hkv, d), device="cuda", dtype=torch.bfloat16, generator=g)
+    v = torch.randn_like(k)
+    for _ in range(2):
+        tx = eng.begin_step(ids)
+        for layer in range(L):
+            eng.step_layer(tx, layer, q, k, v)
+        eng.commit_step(tx)
+    lens = [cache.request_state(r)["seq_len"] for r in ids]
+    tx = eng.begin_step(ids)
+    q_strided = torch.randn((hq, 2, d), device="cuda", dtype=torch.bfloat16,
+                            generator=g).transpose(0, 1)
+    with pytest.raises(ValueError, match="q must be a contiguous"):
+        eng.step_layer(tx, 0, q_strided, k, v)
+    assert [cache.request_state(r)["seq_len"] for r in ids] == lens
+    tx = eng.begin_step(ids)
+    eng.step_layer(tx, 0, q, k, v)
+    with pytest.raises(ValueError, match="k and v must be contiguous"):
+        eng.step_layer(tx, 1, q, k, v.transpose(1, 2).contiguous().transpose(1, 2))
+    assert [cache.request_state(r)["seq_len"] for r in ids] == lens
+    tx = eng.begin_step(ids)
+    for layer in range(L):
+        res = eng.step_layer(tx, layer, q, k, v)
+    eng.commit_step(tx)
+    torch.cuda.synchronize()
+    assert torch.isfinite(res.output.float()).all()
+    assert [cache.request_state(r)["seq_len"] for r in ids] == [n + 1 for n in lens]
