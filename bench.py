@@ -42,7 +42,7 @@ METRIC = ("paged decode attn p50 µs & HBM GB/s (% of peak), B8 ctx2048; "
           "tok/s at 1–8 GPUs")
 C2 = dict(batch=8, hq=16, hkv=2, d=128, bs=32, ctx=2048, pool_factor=2)
 NUM_POOLS = 12
-E2E_STEPS = 2400  # end-to-end steps timed (a multiple of NUM_POOLS and of the two streams)
+E2E_STEPS = 2400  # end-to-end steps timed (a multiple of NUM_POOLS and of the four streams)
 
 
 def _peaks():
@@ -268,9 +268,10 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
     # seq_lens sit in one pinned host arena (the way a serving host stages a
     # step's inputs) and cross in one H2D copy; paged_decode_attention_into
     # writes a preallocated output, which is read back by one D2H copy.
-    # Consecutive steps alternate between two streams with their own device
-    # buffers (double buffering), so one step's copies overlap the other's
-    # kernel; a step's three operations stay in order on its stream, and each
+    # Consecutive steps rotate over four streams with their own device
+    # buffers, so one step's copies overlap the other steps' kernels (a
+    # step's H2D -> decode -> D2H chain is latency-bound at about 25 us on its
+    # own); a step's three operations stay in order on its stream, and each
     # stream has its own decode workspace.  The step count does not depend on
     # --steps (E2E_STEPS), so start-up does not dominate; every step's output
     # lands in its own pinned buffer and all of them are checked afterwards.
@@ -301,7 +302,7 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
             hbt_v.copy_(p["bt"].cpu())
             hsl_v.copy_(sl.cpu())
             harena.append(h)
-        nbuf = 2
+        nbuf = 4
         e2e_streams = [torch.cuda.Stream(device) for _ in range(nbuf)]
         darenas = [torch.empty(arena_nb, dtype=torch.uint8, device=device) for _ in range(nbuf)]
         dviews = [views(x) for x in darenas]
@@ -318,7 +319,7 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
 
         def e2e_step(i):
             j = i % NUM_POOLS
-            bb = i & 1
+            bb = i % nbuf
             set_stream(e2e_streams[bb])
             dq, dbt, dsl = dviews[bb]
             darenas[bb].copy_(harena[j], non_blocking=True)
@@ -360,8 +361,8 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
             "steps": e2e_steps,
             "us_per_step": e2e_ms * 1000.0 / e2e_steps,
             "api": "flashdec_b200.paged_decode_attention_into; q, block tables and seq_lens in one "
-                   "pinned host arena, one H2D and one D2H copy per step; steps alternate "
-                   "between two streams with their own device buffers and workspaces",
+                   "pinned host arena, one H2D and one D2H copy per step; steps rotate over "
+                   "four streams with their own device buffers and workspaces",
             "check": f"all {e2e_steps} host outputs equal the device-resident decode of their inputs",
             "timing": "wall clock between device-wide synchronisations",
         }
@@ -480,22 +481,74 @@ def run_ragged(torch, dist, device, rank, world, stream, args, batch=64):
     stream.synchronize()
     ms = e0.elapsed_time(e1) / steps
     local_bytes = attention_bytes(mine, hq, hkv, d, bs)
-    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    # per-rank time, requests and bytes (every rank's numbers, not rank 0's)
+    mine_t = torch.tensor([ms, len(mine), local_bytes], device=device, dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
+        every = torch.empty((world, 3), device=device, dtype=torch.float64)
+        dist.all_gather_into_tensor(every, mine_t)
+    else:
+        every = mine_t.view(1, 3)
+    every = every.cpu().tolist()
+    rank_ms = [r[0] for r in every]
+    max_ms = max(rank_ms)
     peak, _ = _peaks()
-    return {
+    rank_gbs = [r[2] / (r[0] / 1000.0) / 1e9 for r in every]
+    res = {
         "workload": "BASELINE c4: B64 Llama-3-8B attention (32q/8kv, D128, bs16), seq log-uniform [512,131072]",
         "tokens_per_step": len(lens),
         "ms_per_step_max_rank": max_ms,
+        "ms_per_step_mean_rank": sum(rank_ms) / world,
+        "max_over_mean": max_ms / (sum(rank_ms) / world),
         "tokens_per_s": len(lens) / (max_ms / 1000.0),
-        "rank0_requests": len(mine),
-        "rank0_hbm_gbs": local_bytes / (ms / 1000.0) / 1e9,
-        "rank0_frac_of_peak": local_bytes / (ms / 1000.0) / 1e9 / peak,
+        "rank_ms": rank_ms,
+        "rank_requests": [int(r[1]) for r in every],
+        "rank_hbm_gbs": rank_gbs,
+        "rank_frac_of_peak": [g / peak for g in rank_gbs],
         "steps": steps,
-        "scaling": "strong (fixed 64-request batch split across ranks)",
+        "scaling": "strong (fixed 64-request batch split across ranks, LPT by length)",
     }
+    if world > 1:
+        res["gather"] = _timed_gather(torch, dist, device, stream, out, shards, rank, world)
+    return res
+
+
+def _timed_gather(torch, dist, device, stream, out, shards, rank, world, reps=20):
+    """NCCL all-gather of the ranks' [B_r, Hq, D] outputs to the global batch
+    (flashdec_b200.sharding.gather_outputs), timed with CUDA events (max over
+    ranks) and checked once: rank 0 compares an fp64 checksum of every
+    shard's rows in the gathered batch with the checksum its owner computed
+    locally."""
+    from flashdec_b200.sharding import gather_outputs
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            glob = gather_outputs(out, shards, rank)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            glob = gather_outputs(out, shards, rank)
+        e1.record(stream)
+    stream.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / reps], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    local = out.double().sum().view(1)
+    sums = torch.empty(world, device=device, dtype=torch.float64)
+    dist.all_gather_into_tensor(sums, local)
+    ok = True
+    if rank == 0:
+        for r, idx in enumerate(shards):
+            got = glob[torch.as_tensor(idx, device=device)].double().sum()
+            ok = ok and bool(got == sums[r])
+    flag = torch.tensor([0 if ok else 1], device=device, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+    if int(flag.item()):
+        raise RuntimeError("gathered outputs differ from the ranks' local outputs")
+    rows = max(len(s) for s in shards)
+    return {"us_max_rank": float(t.item()),
+            "bytes_per_rank": rows * out.shape[1] * out.shape[2] * out.element_size(),
+            "collective": "all_gather_into_tensor (NCCL), padded to the largest shard",
+            "check": "fp64 checksum of every shard's gathered rows equals its owner's"}
 
 
 def _graph_time_us(torch, stream, fn, reps, inner=1):
@@ -711,10 +764,14 @@ def run_c5(torch, device, args, num_layers=36, num_requests=16, prefix_tokens=40
                     generator=g)
     v = torch.randn_like(k)
 
+    # per-layer operands as separate tensors, the way a model hands each
+    # layer's projections to the engine
+    qs, ks, vs = list(q.unbind(0)), list(k.unbind(0)), list(v.unbind(0))
+
     def engine_step():
         tx = eng.begin_step(ids)
         for layer in range(num_layers):
-            eng.step_layer(tx, layer, q[layer], k[layer], v[layer], rotary_dim=d, base=1e6)
+            eng.step_layer(tx, layer, qs[layer], ks[layer], vs[layer], rotary_dim=d, base=1e6)
         return eng.commit_step(tx)
 
     for _ in range(2):

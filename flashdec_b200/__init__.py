@@ -31,13 +31,21 @@ __all__ = [
     "reserve_workspace",
 ]
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
 
 _ENGINE = ("AdmissionResult", "DecodeEngine", "DecodeLayerResult", "DecodeStepResult",
            "DecodeStepTransaction")
 
 
 def __getattr__(name):
+    # resolved once, then a plain module attribute (no import per access:
+    # ``flashdec_b200.paged_decode_attention_into`` sits on the per-step path)
+    value = _resolve(name)
+    globals()[name] = value
+    return value
+
+
+def _resolve(name):
     if name in _ENGINE:
         from . import engine
 

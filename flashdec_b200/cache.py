@@ -17,6 +17,7 @@ rebuilds those tensors on every layer write (cache.py:592, :1043-1076).
 from __future__ import annotations
 
 import ctypes
+import itertools
 import math
 import os
 from dataclasses import dataclass, replace
@@ -45,6 +46,67 @@ class KVTokenTransactionView:
     state: str
 
 
+class _PinnedStaging:
+    """Reused pinned host memory for the per-token metadata uploads.
+
+    ``tensor.pin_memory()`` per upload asks torch's caching host allocator for
+    a block, and its blocks are released only once their copy has completed:
+    with the device a few steps behind the host (the normal state of a decode
+    loop) every upload pins new memory, which costs about 100 us.  Here one
+    pinned arena of ``slots`` equal slots is allocated up front and its slots
+    are rewritten in turn; before a slot is reused the host waits for the
+    event recorded after that slot's last copy (normally long complete).  The
+    wait, the copy and the event live in the C++ host path.  An upload larger
+    than a slot re-allocates the arena with larger slots (after every pending
+    copy of the old one has completed)."""
+
+    _ids = itertools.count(1)
+
+    def __init__(self, slots=64):
+        from . import _lib
+
+        self.hp = _lib.load_hostpath()
+        self.ring = next(self._ids)
+        self.slots = slots
+        self.slot_bytes = 0
+        self.arena = None
+        self.host = None
+        self.base = 0
+        self.next = 0
+
+    def __del__(self):
+        try:
+            self.hp.staging_release(self.ring)
+        except Exception:  # interpreter shutdown
+            pass
+
+    def _grow(self, nbytes):
+        for i in range(self.slots if self.arena is not None else 0):
+            self.hp.staging_wait(self.ring, self.slots, i)
+        size = max(16384, 1 << (nbytes - 1).bit_length())
+        self.arena = torch.empty(self.slots * size, dtype=torch.uint8, pin_memory=True)
+        self.host = self.arena.numpy()
+        self.base = self.arena.data_ptr()
+        self.slot_bytes = size
+        self.next = 0
+
+    def upload(self, array, device):
+        """Device copy (uint8, on the device's current stream) of a numpy array."""
+        if torch._C._cuda_getDevice() != device.index:
+            with torch.cuda.device(device):
+                return self.upload(array, device)
+        raw = np.ascontiguousarray(array).reshape(-1).view(np.uint8)
+        n = raw.size
+        if n > self.slot_bytes:
+            self._grow(n)
+        i = self.next
+        self.next = (i + 1) % self.slots
+        self.hp.staging_wait(self.ring, self.slots, i)
+        off = i * self.slot_bytes
+        self.host[off:off + n] = raw
+        return self.hp.staging_copy(self.ring, self.slots, i, self.base + off, n)
+
+
 class _DeviceMeta:
     """Device copies of one transaction's metadata: ``kernel`` tensors are
     private (the kernels read only these), ``public`` ones back the views.
@@ -56,7 +118,8 @@ class _DeviceMeta:
     :class:`_BlockTableCache` and is shared with earlier transactions while
     its rows are unchanged."""
 
-    def __init__(self, device, positions, locations, table, block_size, cascade=None):
+    def __init__(self, device, positions, locations, table, block_size, cascade=None,
+                 staging=None):
         n = len(positions)
         self.cascade = cascade  # _native.CascadeGroups of the batch's shared prefixes, or None
         packed = np.empty(4 * n * 8 + n * 4, np.uint8)
@@ -66,17 +129,30 @@ class _DeviceMeta:
         i64[2 * n:3 * n] = [o for _, o in locations]
         i64[3 * n:] = i64[n:2 * n] * block_size + i64[2 * n:3 * n]
         packed[4 * n * 8:].view(np.int32)[:] = i64[:n] + 1
-        buf = torch.from_numpy(packed)
         if device.type == "cuda":
-            buf = buf.pin_memory().to(device, non_blocking=True)
+            buf = staging.upload(packed, device)
+            self._unpack = staging.hp.unpack_meta
+        else:
+            buf = torch.from_numpy(packed)
+            self._unpack = _unpack_meta
         self._packed, self.block_tables = buf, table
         (self.positions, self.block_ids, self.offsets, self.slots,
-         self.eff_seq_lens) = _unpack_meta(buf, n)
-        self.public = self.snapshot()
+         self.eff_seq_lens) = self._unpack(buf, n)
+        self._public = None
+
+    @property
+    def public(self):
+        """The transaction's public metadata: one copy per token, taken on
+        first use (kernels read the internal buffers, which callers never
+        see)."""
+        pub = self._public
+        if pub is None:
+            pub = self._public = self.snapshot()
+        return pub
 
     def snapshot(self):
         """Fresh copies of the metadata (two copies: packed integers, table)."""
-        pub = _unpack_meta(self._packed.clone(), len(self.positions))
+        pub = self._unpack(self._packed.clone(), len(self.positions))
         return dict(positions=pub[0], physical_block_ids=pub[1], block_offsets=pub[2],
                     effective_seq_lens=pub[4], block_tables=self.block_tables.clone())
 
@@ -84,9 +160,8 @@ class _DeviceMeta:
 def _unpack_meta(buf, n):
     """(positions, block ids, offsets, slots) int64 and effective lengths
     int32 views of a packed metadata buffer."""
-    i64 = buf[:4 * n * 8].view(torch.int64)
-    return (i64[:n], i64[n:2 * n], i64[2 * n:3 * n], i64[3 * n:],
-            buf[4 * n * 8:].view(torch.int32))
+    pos, bid, off, slot = buf[:4 * n * 8].view(torch.int64).view(4, n).unbind(0)
+    return pos, bid, off, slot, buf[4 * n * 8:].view(torch.int32)
 
 
 class _BlockTableCache:
@@ -106,7 +181,7 @@ class _BlockTableCache:
         self.host = None
         self.table = None
 
-    def get(self, device, ids, block_lists):
+    def get(self, device, ids, block_lists, staging=None):
         n = len(block_lists)
         width = max(1, max(map(len, block_lists)))
         if self.ids == ids and self.host is not None and self.host.shape[1] == width:
@@ -121,11 +196,10 @@ class _BlockTableCache:
             row = block_lists[i]
             host[i, :len(row)] = row
             host[i, len(row):] = -1
-        table = torch.from_numpy(host)
         if device.type == "cuda":
-            table = table.pin_memory().to(device, non_blocking=True)
+            table = staging.upload(host, device).view(torch.int32).view(host.shape)
         else:
-            table = table.clone()
+            table = torch.from_numpy(host).clone()
         self.ids, self.rows, self.host, self.table = ids, [list(b) for b in block_lists], host, table
         return table
 
@@ -334,6 +408,7 @@ class PagedKVCache:
         self.v_cache = torch.zeros_like(self.k_cache)
         self.device = self.k_cache.device
         self._tables = _BlockTableCache()
+        self._staging_ring = None  # _PinnedStaging, created by the first CUDA upload
         self._cascades = _CascadeCache()
 
     # ----------------------------------------------------------- lifecycle
@@ -454,6 +529,13 @@ class PagedKVCache:
         self._ledger.advance_lengths(ids)
         return q_rot, self.block_tables(ids)
 
+    def _staging(self):
+        if self.device.type != "cuda":
+            return None
+        if self._staging_ring is None:
+            self._staging_ring = _PinnedStaging()
+        return self._staging_ring
+
     # --------------------------------------------------------- transactions
     def begin_token(self, request_ids):
         """Reserve one token location per request for every layer; seq_len is
@@ -462,12 +544,13 @@ class PagedKVCache:
         tx = self._ledger.begin_token(ids)
         try:
             table = self._tables.get(self.device, ids,
-                                     [self._ledger.requests[r].block_ids for r in ids])
+                                     [self._ledger.requests[r].block_ids for r in ids],
+                                     self._staging())
             cascade = (self._cascades.get(self.device, ids, self._ledger.requests,
                                           self.block_size)
                        if self.device.type == "cuda" and _cascade_enabled() else None)
             tx.device_view = _DeviceMeta(self.device, tx.positions, tx.locations, table,
-                                         self.block_size, cascade)
+                                         self.block_size, cascade, self._staging())
         except Exception:
             self._ledger.abort_token(tx)
             raise
@@ -574,10 +657,6 @@ class PagedKVCache:
         view = replace(self._view(state), state="aborted")
         self._ledger.abort_token(state)
         return view
-
-    def _transaction_snapshot(self, transaction):
-        """Fresh copies of an open transaction's public metadata tensors."""
-        return self._require_open_transaction(transaction).device_view.snapshot()
 
     def transaction_view(self, transaction):
         state = self._require_transaction(transaction)

@@ -2234,6 +2234,18 @@ int validate(const fd_paged_decode_args* a) {
 constexpr int kSplitMaxTilesPerCta = 32;
 constexpr int kSplitMinTilesPerCta = 2;
 constexpr int kWaveSplitCap = 14;
+constexpr int kWaveBalancedMaxTiles = 64;
+
+// FLASHDEC_B200_BALANCED_MAX_TILES=n: a batch takes the balanced split plan
+// while pairs x tiles <= SMs x n (tuning sweeps; default kSplitMaxTilesPerCta)
+int balanced_max_tiles_per_cta() {
+  static const int n = [] {
+    const char* v = std::getenv("FLASHDEC_B200_BALANCED_MAX_TILES");
+    const int x = v ? std::atoi(v) : 0;
+    return x > 0 ? x : kSplitMaxTilesPerCta;
+  }();
+  return n;
+}
 constexpr int kWaveLongTiles = 12;
 
 struct Plan {
@@ -2255,10 +2267,13 @@ Plan make_plan(const fd_paged_decode_args& a, const Derived& dv, const DeviceInf
     return pl;
   }
   const int64_t nsm = dev.num_sms;
-  if (a.max_ctas <= 0 && pairs <= nsm && pairs * pl.cap_tiles <= nsm * kSplitMaxTilesPerCta) {
+  const bool wave = wave_enabled() && a.epilogue == FD_EPILOGUE_FUSED;
+  const int64_t work = pairs * pl.cap_tiles;
+  if (a.max_ctas <= 0 && pairs <= nsm &&
+      work <= nsm * (wave ? kWaveBalancedMaxTiles : balanced_max_tiles_per_cta())) {
     int64_t s = nsm / pairs;
     s = std::min<int64_t>(s, std::max(1, pl.cap_tiles / kSplitMinTilesPerCta));
-    if (wave_enabled() && a.epilogue == FD_EPILOGUE_FUSED) {
+    if (wave) {
       // One-wave kernel (two CTAs fit an SM): clusters above 14 CTAs cost
       // more in residency than they add; once a split would hold 12 tiles or
       // more, about 1.3 CTAs per SM beat one (measured over B1-B16,
@@ -2268,10 +2283,19 @@ Plan make_plan(const fd_paged_decode_args& a, const Derived& dv, const DeviceInf
         s = std::max<int64_t>(s, std::min<int64_t>(kWaveSplitCap, nsm * 13 / 10 / pairs));
       if (wave_splits_override() > 0) s = wave_splits_override();
     }
-    pl.splits = static_cast<int>(std::max<int64_t>(1, s));
-    pl.balanced = 1;
-    pl.grid = static_cast<int>(pairs * pl.splits);
-    return pl;
+    s = std::max<int64_t>(1, s);
+    // Past the plain limit the even split pays only while its CTAs cover
+    // every SM (B16 x 5k tokens: 21.3 us against 26.8 us for stream-K; B4 x
+    // 32k, 112 CTAs: 44.9 against 35.2).  The split is even over the block
+    // table width, not the true lengths: a ragged batch in this range can
+    // run up to about twice the stream-K time, which bounds the range.
+    const bool fits = work <= nsm * balanced_max_tiles_per_cta() || pairs * s >= nsm;
+    if (fits) {
+      pl.splits = static_cast<int>(s);
+      pl.balanced = 1;
+      pl.grid = static_cast<int>(pairs * pl.splits);
+      return pl;
+    }
   }
   pl.splits = 0;
   // Two resident CTAs per SM when a ring of at least 4 stages fits in half

@@ -20,6 +20,11 @@
 //    shape checks, the output allocation and one fd_paged_decode (or
 //    fd_cascade_decode) on the current stream.
 //
+//  * staging_wait / staging_copy / unpack_meta: the engine's per-token
+//    metadata upload (one copy from a reused pinned slot, one event per slot)
+//    and its split into typed views, each one call instead of several torch
+//    operations.
+//
 // The entry points are taken as addresses from the already-loaded
 // libflashdec_b200.so (set_entry_points), so both paths call the same
 // library.  Every function runs with the GIL held, which serialises the
@@ -32,7 +37,9 @@
 #include <array>
 #include <cstdint>
 #include <cstring>
+#include <stdexcept>
 #include <unordered_map>
+#include <vector>
 
 #include "flashdec_b200.h"
 
@@ -185,6 +192,74 @@ py::object layer_run(int64_t args, int64_t cascade, const at::Tensor& q, const a
   return py::cast(out);
 }
 
+// ---- pinned staging of the engine's per-token metadata -------------------
+// One event per slot of a Python-owned pinned ring (flashdec_b200.cache):
+// staging_wait blocks until the slot's previous copy has completed,
+// staging_copy enqueues the slot's bytes to a new device buffer on the current
+// stream and records the slot's event.  Rings are numbered by the caller.
+struct StagingRing {
+  int device = -1;
+  std::vector<cudaEvent_t> events;
+  std::vector<char> recorded;
+};
+std::unordered_map<int64_t, StagingRing> g_rings;
+
+StagingRing& ring_of(int64_t ring, int64_t slots, int64_t slot) {
+  if (slots <= 0 || slot < 0 || slot >= slots) throw py::value_error("staging slot out of range");
+  StagingRing& r = g_rings[ring];
+  if (static_cast<int64_t>(r.events.size()) != slots) {
+    for (cudaEvent_t e : r.events) cudaEventDestroy(e);
+    r.events.assign(static_cast<size_t>(slots), nullptr);
+    r.recorded.assign(static_cast<size_t>(slots), 0);
+    r.device = c10::cuda::current_device();
+  }
+  return r;
+}
+
+void staging_wait(int64_t ring, int64_t slots, int64_t slot) {
+  StagingRing& r = ring_of(ring, slots, slot);
+  if (r.recorded[slot]) {
+    const cudaError_t e = cudaEventSynchronize(r.events[slot]);
+    if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+    r.recorded[slot] = 0;
+  }
+}
+
+at::Tensor staging_copy(int64_t ring, int64_t slots, int64_t slot, int64_t host_ptr,
+                        int64_t nbytes) {
+  StagingRing& r = ring_of(ring, slots, slot);
+  const int dev = c10::cuda::current_device();
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  at::Tensor out = at::empty({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev));
+  cudaError_t e = cudaMemcpyAsync(out.data_ptr(), reinterpret_cast<const void*>(host_ptr),
+                                  static_cast<size_t>(nbytes), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess && !r.events[slot])
+    e = cudaEventCreateWithFlags(&r.events[slot], cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventRecord(r.events[slot], stream);
+  if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+  r.recorded[slot] = 1;
+  return out;
+}
+
+void staging_release(int64_t ring) {
+  auto it = g_rings.find(ring);
+  if (it == g_rings.end()) return;
+  for (cudaEvent_t e : it->second.events)
+    if (e) cudaEventDestroy(e);
+  g_rings.erase(it);
+}
+
+// (positions, block ids, offsets, slots) int64 and effective lengths int32
+// views of a packed uint8 metadata buffer of n rows: [4 n int64 | n int32].
+std::vector<at::Tensor> unpack_meta(const at::Tensor& buf, int64_t n) {
+  at::Tensor i64 = buf.narrow(0, 0, 32 * n).view(at::kLong);
+  std::vector<at::Tensor> out;
+  out.reserve(5);
+  for (int64_t i = 0; i < 4; ++i) out.push_back(i64.narrow(0, i * n, n));
+  out.push_back(buf.narrow(0, 32 * n, 4 * n).view(at::kInt));
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -197,4 +272,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clear", &clear);
   m.def("table_size", &table_size);
   m.def("layer_run", &layer_run);
+  m.def("staging_wait", &staging_wait);
+  m.def("staging_copy", &staging_copy);
+  m.def("staging_release", &staging_release);
+  m.def("unpack_meta", &unpack_meta);
 }

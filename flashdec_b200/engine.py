@@ -267,12 +267,14 @@ class DecodeEngine:
             self._backpressure_count += 1
             raise RuntimeError("insufficient physical blocks to begin decode step")
         ctx = self.cache.begin_token(ids)
-        snap = self.cache._transaction_snapshot(ctx)  # the handle's own copies
+        # The view's tensors are already this token's public copies (the
+        # kernels read the cache's internal buffers), so the handle takes them
+        # as they are: one device copy of the metadata per token.
         handle = DecodeStepTransaction(
             transaction_id=ctx.transaction_id, engine_version=self._state_version + 1,
-            request_ids=tuple(ids), positions=snap["positions"],
-            physical_block_ids=snap["physical_block_ids"], block_offsets=snap["block_offsets"],
-            block_tables=snap["block_tables"], effective_seq_lens=snap["effective_seq_lens"])
+            request_ids=tuple(ids), positions=ctx.positions,
+            physical_block_ids=ctx.physical_block_ids, block_offsets=ctx.block_offsets,
+            block_tables=ctx.block_tables, effective_seq_lens=ctx.effective_seq_lens)
         self._bump_state_version()
         self._open = _OpenStep(handle, ctx, needed)
         return handle

@@ -65,6 +65,16 @@ def _launch_prepared(prep, q, k_cache, v_cache, block_tables, seq_lens, out):
                         _native.stream_handle(dev))
 
 
+_FAST = None  # (C++ decode_into, its miss code), bound on first use
+
+
+def _fast_entry():
+    global _FAST
+    hp = _lib.load_hostpath()
+    _FAST = (hp.decode_into, hp.MISS)
+    return _FAST
+
+
 def _register(prep, q, k_cache, v_cache, block_tables, seq_lens, out):
     """Hand the struct that just launched (bound to the current stream's
     workspace, which ``prep`` keeps alive while it is in ``_PREPARED``) to
@@ -232,17 +242,18 @@ def paged_decode_attention_into(
     """
     # The call with every scalar at its default goes to the C++ host path
     # first: a signature it has seen on this stream launches there.
-    default_call = (sm_scale is None and block_size is None and num_stages is None
-                    and split_kv_workspace is None and append_k is None and append_v is None
-                    and slot_mapping is None and type(num_warps) is int and num_warps == 2
-                    and type(num_splits) is int and num_splits == 1
+    # (the chained identities hold only when all seven are None)
+    default_call = (sm_scale is block_size is num_stages is split_kv_workspace is append_k
+                    is append_v is slot_mapping is None
+                    and num_warps.__class__ is int and num_warps == 2
+                    and num_splits.__class__ is int and num_splits == 1
                     and kv_layout == "token_major")
     if default_call:
-        hp = _lib.load_hostpath()
+        decode_into, miss = _FAST or _fast_entry()
         try:
-            rc = hp.decode_into(q, k_cache, v_cache, block_tables, seq_lens, out)
+            rc = decode_into(q, k_cache, v_cache, block_tables, seq_lens, out)
         except TypeError:  # not tensors: the checks below raise the reference's errors
-            rc = hp.MISS
+            rc = miss
         if rc == 0:
             return out
         if rc < 0:
