@@ -1199,15 +1199,23 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        # rank 0 prints exactly one JSON line on stdout: NCCL's communicator
-        # set-up lines (INIT: ranks, devices, transports) go to stderr
-        if "NCCL_DEBUG" not in os.environ:
+        # rank 0 prints exactly one JSON line on stdout.  NCCL's communicator
+        # lines (INIT: ranks, devices, transports; teardown) are wanted in the
+        # log, and NCCL writes them to the process's stdout: under torchrun
+        # file descriptor 1 points at stderr for the whole run, and the JSON
+        # line goes to a duplicate of the real stdout taken first.
+        # (the image presets NCCL_DEBUG=VERSION, which prints no INIT lines)
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
             os.environ["NCCL_DEBUG"] = "INFO"
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+        sys.stdout.flush()
+        json_fd = os.dup(1)
+        os.dup2(2, 1)
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    else:
+        json_fd = None
     try:
         res = run_ours(args, rank, world, local_rank)
     finally:
@@ -1215,7 +1223,13 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
     if res is not None:
-        print(json.dumps(res), flush=True)
+        if json_fd is None:
+            print(json.dumps(res), flush=True)
+        else:
+            sys.stdout.flush()
+            os.write(json_fd, (json.dumps(res) + "\n").encode())
+    if json_fd is not None:
+        os.close(json_fd)
 
 
 if __name__ == "__main__":

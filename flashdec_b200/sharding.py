@@ -40,6 +40,27 @@ def shard_loads(lengths: Sequence[int], shards: Sequence[Sequence[int]]) -> list
     return [sum(int(lengths[i]) for i in s) for s in shards]
 
 
+_GATHER_INDEX: dict = {}
+
+
+def _gather_index(shards, rows, device):
+    """(source rows in the padded all-gather buffer, destination rows in the
+    global batch) as device tensors, cached per shard layout and device."""
+    import torch
+
+    key = (tuple(tuple(int(i) for i in s) for s in shards), rows, str(device))
+    idx = _GATHER_INDEX.get(key)
+    if idx is None:
+        src = [r * rows + j for r, s in enumerate(shards) for j in range(len(s))]
+        dst = [int(i) for s in shards for i in s]
+        idx = (torch.tensor(src, dtype=torch.int64, device=device),
+               torch.tensor(dst, dtype=torch.int64, device=device))
+        if len(_GATHER_INDEX) >= 64:
+            _GATHER_INDEX.clear()
+        _GATHER_INDEX[key] = idx
+    return idx
+
+
 def gather_outputs(local_out, shards, rank, group=None, dst=None):
     """Reassemble the global ``[B, Hq, D]`` output from per-rank shards.
 
@@ -47,7 +68,9 @@ def gather_outputs(local_out, shards, rank, group=None, dst=None):
     ``shards[rank]``); rows are padded to the largest shard and exchanged with
     one ``all_gather_into_tensor`` (NCCL over NVLink on GPUs, gloo on CPU).
     Returns the global tensor on every rank, or only on ``dst`` when given
-    (``None`` elsewhere).  All ranks must call it (it is a collective).
+    (``None`` elsewhere).  All ranks must call it (it is a collective).  The
+    row permutation is one ``index_select`` + ``index_copy_`` with index
+    tensors cached per shard layout, so a per-step call adds no host upload.
     """
     import torch
     import torch.distributed as dist
@@ -56,9 +79,12 @@ def gather_outputs(local_out, shards, rank, group=None, dst=None):
     rows = max(len(s) for s in shards)
     total = sum(len(s) for s in shards)
     tail = tuple(local_out.shape[1:])
-    padded = local_out.new_zeros((rows, *tail))
-    if local_out.shape[0]:
-        padded[: local_out.shape[0]] = local_out
+    if local_out.shape[0] == rows and local_out.is_contiguous():
+        padded = local_out
+    else:
+        padded = local_out.new_zeros((rows, *tail))
+        if local_out.shape[0]:
+            padded[: local_out.shape[0]] = local_out
     if dist.get_backend(group) == "gloo":
         parts = [torch.empty_like(padded) for _ in range(world)]
         dist.all_gather(parts, padded, group=group)
@@ -66,11 +92,9 @@ def gather_outputs(local_out, shards, rank, group=None, dst=None):
     else:
         gathered = padded.new_empty((world * rows, *tail))
         dist.all_gather_into_tensor(gathered, padded, group=group)
-        gathered = gathered.view(world, rows, *tail)
     if dst is not None and rank != dst:
         return None
+    src_idx, dst_idx = _gather_index(shards, rows, local_out.device)
     out = local_out.new_empty((total, *tail))
-    for r, idx in enumerate(shards):
-        if idx:
-            out[torch.as_tensor(list(idx), device=out.device)] = gathered[r, : len(idx)]
+    out.index_copy_(0, dst_idx, gathered.reshape(world * rows, *tail).index_select(0, src_idx))
     return out
