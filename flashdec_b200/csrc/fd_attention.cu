@@ -2734,8 +2734,9 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
     bool wtma = true;
     w.num_kv_heads = a->num_kv_heads;
     w.spec_skew = wave_spec_skew();
-    if (D == 128 && a->block_size == 32) {
-      // a contiguous token-major pair of caches: one box per page moves K and V
+    if (D == 128 && (a->block_size == 32 || a->block_size == 16)) {
+      // K and V of a page in one box: a token-major pair of caches with
+      // evenly spaced planes, or vLLM's per-block interleaved planes
       CacheDesc cd;
       cd.base = a->k_cache;
       cd.elem_bytes = 2;
@@ -2746,7 +2747,7 @@ int paged_decode_impl(const fd_paged_decode_args* a, const int* pre_pages, int p
       cd.num_blocks = a->num_blocks;
       for (int i = 0; i < 4; ++i) cd.stride[i] = a->k_stride[i];
       w.kv_box = kv_pair_enabled() &&
-                 get_kv_pair_tensor_map(cd, a->v_cache, a->v_stride, &wk, &w.v_first);
+                 get_kv_pair_tensor_map(cd, a->v_cache, a->v_stride, &wk, &w.v_first, w.pair_m);
     }
     if (D == 128 && a->block_size == 32 && !w.kv_box) {
       for (int plane = 0; plane < 2 && wtma; ++plane) {

@@ -68,11 +68,12 @@ struct MapEntry {
 struct PairKey {
   const void* k;
   const void* v;
-  int is_bf16, num_heads, num_blocks;
+  int is_bf16, num_heads, num_blocks, block_size;
   int64_t stride[4];
   bool operator==(const PairKey& o) const {
     return k == o.k && v == o.v && is_bf16 == o.is_bf16 && num_heads == o.num_heads &&
-           num_blocks == o.num_blocks && std::memcmp(stride, o.stride, sizeof(stride)) == 0;
+           num_blocks == o.num_blocks && block_size == o.block_size &&
+           std::memcmp(stride, o.stride, sizeof(stride)) == 0;
   }
 };
 
@@ -80,6 +81,7 @@ struct PairEntry {
   PairKey key;
   CUtensorMap map;
   int v_first;
+  int m[3];
   uint64_t stamp;
 };
 
@@ -266,28 +268,21 @@ bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]) {
 }
 
 bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_t v_stride[4],
-                            CUtensorMap* out, int* v_first) {
-  if (k.elem_bytes != 2 || k.head_dim != 128 || k.block_size != 32) return false;
+                            CUtensorMap* out, int* v_first, int m[3]) {
+  if (k.elem_bytes != 2 || k.head_dim != 128 || (k.block_size != 32 && k.block_size != 16))
+    return false;
   for (int i = 0; i < 4; ++i)
     if (k.stride[i] != v_stride[i]) return false;
   if (k.stride[3] != 1) return false;
-  // planes (block, head) evenly spaced: a single plane index blk * heads + head
-  const int64_t plane = k.num_heads == 1 ? k.stride[0] : k.stride[1];
-  if (k.num_heads > 1 && k.stride[0] != plane * k.num_heads) return false;
   const int64_t tok_bytes = k.stride[2] * 2;
-  const int64_t plane_bytes = plane * 2;
-  if (tok_bytes % 16 || plane_bytes % 16 || tok_bytes <= 0 || plane_bytes <= 0) return false;
+  if (tok_bytes % 16 || tok_bytes <= 0) return false;
   const uintptr_t kb = reinterpret_cast<uintptr_t>(k.base);
   const uintptr_t vb = reinterpret_cast<uintptr_t>(v_base);
   if (kb % 16 || vb % 16 || kb == vb) return false;
   const uintptr_t lo = kb < vb ? kb : vb;
   const uint64_t delta = kb < vb ? vb - kb : kb - vb;
   if (delta % 16 || delta >= (uint64_t(1) << 40)) return false;
-  const int64_t planes = static_cast<int64_t>(k.num_blocks) * k.num_heads;
-  // the plane axis must not reach into the other allocation's range: one
-  // allocation's last plane ends before the other starts (delta covers it)
-  if (static_cast<uint64_t>(planes) * plane_bytes > delta) return false;
-  PairKey key{k.base, v_base, k.is_bf16, k.num_heads, k.num_blocks,
+  PairKey key{k.base, v_base, k.is_bf16, k.num_heads, k.num_blocks, k.block_size,
               {k.stride[0], k.stride[1], k.stride[2], k.stride[3]}};
   {
     std::lock_guard<std::mutex> lock(g_map_mu);
@@ -296,16 +291,48 @@ bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_
         e.stamp = ++g_map_clock;
         *out = e.map;
         *v_first = e.v_first;
+        for (int i = 0; i < 3; ++i) m[i] = e.m[i];
         return true;
       }
     }
   }
+  const cuuint64_t bs = static_cast<cuuint64_t>(k.block_size);
+  const int64_t head_bytes = k.num_heads == 1 ? 128 : k.stride[1] * 2;
+  cuuint64_t dims[5], strides[4];
+  int mm[3];
+  // planes apart: (block, head) planes evenly spaced in each allocation
+  const int64_t plane = k.num_heads == 1 ? k.stride[0] : k.stride[1];
+  const int64_t planes = static_cast<int64_t>(k.num_blocks) * k.num_heads;
+  const bool apart = (k.num_heads == 1 || k.stride[0] == plane * k.num_heads) && plane > 0 &&
+                     (plane * 2) % 16 == 0 && static_cast<uint64_t>(planes) * plane * 2 <= delta;
+  // interleaved: block stride twice the K -> V distance, a block's K plane
+  // (all heads and tokens) inside that distance
+  const int64_t k_extent = ((bs - 1) * k.stride[2] + (k.num_heads - 1) * (k.num_heads > 1 ? k.stride[1] : 0) +
+                            k.head_dim) * 2;
+  const bool interleaved = !apart && static_cast<uint64_t>(k.stride[0]) * 2 == 2 * delta &&
+                           head_bytes % 16 == 0 && head_bytes > 0 &&
+                           static_cast<uint64_t>(k_extent) <= delta;
+  if (apart) {
+    dims[0] = 64u; dims[1] = bs; dims[2] = 2u; dims[3] = static_cast<cuuint64_t>(planes); dims[4] = 2u;
+    strides[0] = static_cast<cuuint64_t>(tok_bytes);
+    strides[1] = 128u;
+    strides[2] = static_cast<cuuint64_t>(plane * 2);
+    strides[3] = static_cast<cuuint64_t>(delta);
+    mm[0] = k.num_heads; mm[1] = 1; mm[2] = 0;
+  } else if (interleaved) {
+    dims[0] = 64u; dims[1] = bs; dims[2] = 2u; dims[3] = static_cast<cuuint64_t>(k.num_heads);
+    dims[4] = 2u * static_cast<cuuint64_t>(k.num_blocks);
+    strides[0] = static_cast<cuuint64_t>(tok_bytes);
+    strides[1] = 128u;
+    strides[2] = static_cast<cuuint64_t>(head_bytes);
+    strides[3] = static_cast<cuuint64_t>(delta);
+    mm[0] = 0; mm[1] = 1; mm[2] = 2;
+  } else {
+    return false;
+  }
   resolve_encoder();
   if (!g_encode) return false;
-  cuuint64_t dims[5] = {64u, 32u, 2u, static_cast<cuuint64_t>(planes), 2u};
-  cuuint64_t strides[4] = {static_cast<cuuint64_t>(tok_bytes), 128u,
-                           static_cast<cuuint64_t>(plane_bytes), static_cast<cuuint64_t>(delta)};
-  cuuint32_t box[5] = {64u, 32u, 2u, 1u, 2u};
+  cuuint32_t box[5] = {64u, static_cast<cuuint32_t>(bs), 2u, 1u, 2u};
   cuuint32_t estride[5] = {1u, 1u, 1u, 1u, 1u};
   CUtensorMap map;
   const CUresult r = g_encode(&map,
@@ -317,6 +344,7 @@ bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_
   if (r != CUDA_SUCCESS) return false;
   *out = map;
   *v_first = vb < kb ? 1 : 0;
+  for (int i = 0; i < 3; ++i) m[i] = mm[i];
   std::lock_guard<std::mutex> lock(g_map_mu);
   if (g_pairs.size() >= kMapCacheSize) {
     auto oldest = std::min_element(g_pairs.begin(), g_pairs.end(),
@@ -325,7 +353,7 @@ bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_
                                    });
     g_pairs.erase(oldest);
   }
-  g_pairs.push_back(PairEntry{key, map, *v_first, ++g_map_clock});
+  g_pairs.push_back(PairEntry{key, map, *v_first, {mm[0], mm[1], mm[2]}, ++g_map_clock});
   return true;
 }
 

@@ -47,16 +47,23 @@ struct CacheDesc {
 // be described by a tensor map.
 bool get_cache_tensor_map(const CacheDesc& d, CUtensorMap* out, int perm[4]);
 
-// One tensor map over both planes of a pair of caches with head_dim 128 and
-// 32-token pages whose (block, head) planes are contiguous and evenly spaced
-// (block stride = heads x head stride, unit dim stride): dims [64 dims, 32
-// tokens, 2 halves, block * heads + head, 2 (K, V)] with the last axis
-// spanning the two allocations (stride |v - k|), box [64, 32, 2, 1, 2], 128B
-// swizzle.  One copy then moves a page's K and V (16 KB) as [plane][half]
-// [32 tokens][64 dims]; *v_first is set when V's allocation comes first
-// (plane 0 is V).  Returns false when the layout does not qualify.
+// One tensor map over the K and V planes of a cache pair with head_dim 128
+// and 16- or 32-token pages, box [64 dims, bs tokens, 2 halves, 1, 2] with the
+// 128B swizzle: one copy moves a page's K and V (bs x 512 bytes) as
+// [plane][half][bs tokens][64 dims].  Two layouts qualify (unit dim stride,
+// equal K and V strides):
+//  * planes apart: each allocation's (block, head) planes contiguous and
+//    evenly spaced (block stride = heads x head stride); dims [64, bs, 2,
+//    blocks * heads, 2] with the last axis spanning the two allocations
+//    (stride |v - k|): page (blk, head) at coordinates (blk * heads + head, 0);
+//  * planes interleaved per block (vLLM's [block, 2, bs, heads, dim] cache:
+//    block stride = 2 |v - k|, a block's K within |v - k|): dims [64, bs, 2,
+//    heads, 2 * blocks]: page (blk, head) at (head, 2 * blk).
+// The page's coordinates on the last two axes are blk * m[0] + head * m[1]
+// and blk * m[2].  *v_first is set when the plane at the lower address is V.
+// Returns false when the layout does not qualify.
 bool get_kv_pair_tensor_map(const CacheDesc& k, const void* v_base, const int64_t v_stride[4],
-                            CUtensorMap* out, int* v_first);
+                            CUtensorMap* out, int* v_first, int m[3]);
 
 // FD_OK, or FD_ERR_CUDA with the message kept for fd_error_string.
 int cuda_status(cudaError_t e);

@@ -256,7 +256,9 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
           // one TMA prefetch per page through the K + V pair map (cheaper to
           // issue than 256 line prefetches)
           if (lane == 0) {
-            tma_prefetch_5d(&tmap_k, 0, 0, 0, static_cast<int>(bj) * p.num_kv_heads + kv_head, 0);
+            tma_prefetch_5d(&tmap_k, 0, 0, 0,
+                            static_cast<int>(bj) * p.pair_m[0] + kv_head * p.pair_m[1],
+                            static_cast<int>(bj) * p.pair_m[2]);
           }
           continue;
         }
@@ -330,12 +332,16 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     // on the SM, and an instruction issuing many costs far less per operation
     // than one issuing a few.
     auto issue = [&](int i0, int np, uint32_t pages, int blk, uint64_t* bars) {
-      if (D == 128 && kPageRows == 0 && p.kv_box) {
+      if (D == 128 && (kPageRows == 0 || kPageRows == 16) && p.kv_box) {
+        // one box per page: K and V of the page, [plane][half][bs][64]; the
+        // pages of a tile follow one another in the stage (16-token pages:
+        // page j at j x 8 KB, see the consumer's page_pair)
         if (lane < np && ((pages >> lane) & 1u)) {
           const int i = i0 + (lane >> ppt_shift);
-          tma_load_5d(smem_u32(stages + (i % NST) * SM::kStageBytes), &tmap_k,
+          const int j = lane & (ppt - 1);  // page of the tile
+          tma_load_5d(smem_u32(stages + (i % NST) * SM::kStageBytes) + j * (bs * 512), &tmap_k,
                       smem_u32(&bars[i % kWaveTileBars]), 0, 0, 0,
-                      blk * p.num_kv_heads + kv_head, 0, policy);
+                      blk * p.pair_m[0] + kv_head * p.pair_m[1], blk * p.pair_m[2], policy);
         }
         return;
       }
@@ -615,9 +621,21 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     v_sw[j] = static_cast<uint32_t>((((2 * j) + (mi & 1)) ^ r8) << 4);
   }
 
-  // K and V regions of a stage (swapped when the pair map's first plane is V)
-  const uint32_t koff = (p.kv_box && p.v_first) ? SM::kHalves * SM::kHalfBytes : 0u;
-  const uint32_t voff = SM::kHalves * SM::kHalfBytes - koff;
+  // K and V regions of a stage (swapped when the pair map's first plane is V).
+  // Separate planes or 32-token pair boxes: K's [half][32][64] then V's.
+  // 16-token pair boxes (page_pair): each page's K then V, [page][plane]
+  // [half][16][64], so 16 rows (one page) are 8 KB apart and V sits 4 KB
+  // after K.
+  const bool page_pair = kPageRows == 16 && p.kv_box;
+  const uint32_t kv_span = page_pair ? static_cast<uint32_t>(kPageRows * 256)
+                                     : static_cast<uint32_t>(SM::kHalves * SM::kHalfBytes);
+  const uint32_t koff = (p.kv_box && p.v_first) ? kv_span : 0u;
+  const uint32_t voff = (p.kv_box ? kv_span : static_cast<uint32_t>(SM::kHalves * SM::kHalfBytes)) - koff;
+  const uint32_t rows16 = SS::kRows16Bytes + (page_pair ? static_cast<uint32_t>(kPageRows * 256) : 0u);
+  // extra bytes before row r's page in the page_pair layout
+  auto page_gap = [&](int r) -> uint32_t {
+    return page_pair ? static_cast<uint32_t>((r / (kPageRows > 0 ? kPageRows : kTile)) * kPageRows * 256) : 0u;
+  };
   float m_run[kNT][2], l_run[kNT][2];
   // o[mt][nt][2 hf + e]: O^T[dim 16 mt + g8 + 8 hf][head nt * 8 + 2 t4 + e]
   float o[kMTD][kNT][4];
@@ -666,7 +684,7 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
         const int r = e / (D / 8);
         const int c = e - r * (D / 8);
         if ((inv >> r) & 1u) {
-          *reinterpret_cast<uint4*>(sb + voff + stage_chunk_offset<kPageRows>(r, c)) =
+          *reinterpret_cast<uint4*>(sb + voff + page_gap(r) + stage_chunk_offset<kPageRows>(r, c)) =
               make_uint4(0u, 0u, 0u, 0u);
         }
       }
@@ -686,8 +704,8 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
       for (int d = lane; d < D; d += 32) {
         const T kv = app_row[d];
         const T vv = app_row[D + d];
-        *reinterpret_cast<T*>(sb + koff + stage_tile_offset<kPageRows>(ra, d)) = kv;
-        *reinterpret_cast<T*>(sb + voff + stage_tile_offset<kPageRows>(ra, d)) = vv;
+        *reinterpret_cast<T*>(sb + koff + page_gap(ra) + stage_tile_offset<kPageRows>(ra, d)) = kv;
+        *reinterpret_cast<T*>(sb + voff + page_gap(ra) + stage_tile_offset<kPageRows>(ra, d)) = vv;
         if (store) {
           kc[d * p.ks3] = kv;
           vc[d * p.vs3] = vv;
@@ -715,7 +733,7 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     auto load_k = [&](int ks, uint32_t (&dst)[2][4]) {
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        ldsm_x4(kbase + k_row + mt * SS::kRows16Bytes + (ks >> 2) * SS::kHalfStride + k_sw[ks & 3],
+        ldsm_x4(kbase + k_row + mt * rows16 + (ks >> 2) * SS::kHalfStride + k_sw[ks & 3],
                 dst[mt][0], dst[mt][1], dst[mt][2], dst[mt][3]);
       }
     };
@@ -739,7 +757,7 @@ __global__ void __launch_bounds__(kWaveThreads, 2)
     auto load_v = [&](int f, uint32_t (&dst)[4]) {
       const int ks = f / kMTD;
       const int mt = f - ks * kMTD;
-      ldsm_x4_t(vbase + v_row + ks * SS::kRows16Bytes + (mt >> 2) * SS::kHalfStride + v_sw[mt & 3],
+      ldsm_x4_t(vbase + v_row + ks * rows16 + (mt >> 2) * SS::kHalfStride + v_sw[mt & 3],
                 dst[0], dst[1], dst[2], dst[3]);
     };
 #pragma unroll

@@ -27,8 +27,11 @@ struct WaveParams {
   int64_t os0, os1, os2;
   int kperm[4], vperm[4];  // tensor-map axis order (0 token, 1 head, 2 block, 3 half)
   // kv_box: the K map is a K + V pair map (get_kv_pair_tensor_map) and one
-  // box moves a page's K and V; v_first: V's plane comes first in the stage
+  // box moves a page's K and V; v_first: V's plane comes first in the stage;
+  // pair_m: page (blk, head) sits at coordinates (blk * pair_m[0] + head *
+  // pair_m[1], blk * pair_m[2]) of the map's last two axes
   int kv_box, v_first, num_kv_heads;
+  int pair_m[3];
   // test hook: added to every speculatively read block id (mod num_blocks)
   // so that the check of the speculative first group must re-load it
   // (FLASHDEC_B200_TEST_SPEC_SKEW; 0 in normal use)
