@@ -440,7 +440,7 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": _traffic_from_profile("paged_decode_c2_ctx2048"),
+            "traffic": _traffic_from_profile("wave_decode_c2_ctx2048"),
             "algorithmic_bytes_per_launch": nbytes,
             "kernel": "fd::wave_decode_kernel<bf16,128,0,1,cluster,plain>",
         },
@@ -677,6 +677,7 @@ def run_vllm_launcher(torch, device, stream, reps=200):
                         "16-token NHD 5-D cache, fused current-token append, graph replay",
             "us_per_step": us, "tokens_per_s": b / (us * 1e-6), "algorithmic_bytes": nbytes,
             "hbm_gbs": gbs, "frac_of_peak": gbs / peak,
+            "traffic": _traffic_from_profile("wave_decode_vllm_b8_ctx2048"),
             "reference_published_us": 38.528,
             "reference_published": "RTX 5070, benchmarks/results/vllm_qwen_attention_summary.md:24"}
 
