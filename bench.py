@@ -17,9 +17,11 @@ collective), ``scaling`` is "weak" and ``value`` is the whole-job tokens/s
 BASELINE config 4 (B=64 Llama-3-8B shape, log-uniform lengths up to 131072)
 sharded across the N ranks by length-balanced (LPT) request sharding.
 
-``--impl reference`` times the reference algorithm on the host CPU (the numpy
-oracle that restates flashdec/paged_reference.py) on the same workload, on
-rank 0 only.
+``--impl reference`` times the reference's own CPU path of the algorithm
+(flashdec/paged_reference.py's paged_decode_attention_ref, imported from the
+reference installed under baseline/_ref; the numpy oracle restating it when
+that install is absent) on the same workload, on all host cores, on rank 0
+only.
 """
 
 from __future__ import annotations
@@ -317,31 +319,28 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
         decode_into = flashdec_b200.paged_decode_attention_into
         set_stream = torch.cuda.set_stream
 
-        # Step i's inputs are staged LOOKAHEAD steps ahead: its H2D copy is
-        # issued before step i - LOOKAHEAD's D2H.  (Issued in step order, a D2H
-        # that waits for its kernel holds the next step's H2D behind it in the
-        # copy queue and the steps run one after another: 15.7-18.3 us per
-        # step against 12.9 us staged.)  Step i's buffers and stream are
-        # i mod nbuf, so a buffer's reuse stays ordered on its own stream.
-        LOOKAHEAD = nbuf - 1
-
-        def stage(i):
-            bb = i % nbuf
-            set_stream(e2e_streams[bb])
-            darenas[bb].copy_(harena[i % NUM_POOLS], non_blocking=True)
+        # Steps are staged ahead: step i's stream and buffers are i mod nbuf,
+        # and right after step i's D2H the same stream takes the H2D of step
+        # i + nbuf (which reuses step i's buffers, in order on that stream).
+        # So every step's inputs are in flight nbuf - 1 steps before its
+        # kernel, and each step switches streams once.  (Issued in step order,
+        # a D2H that waits for its kernel holds the next step's H2D behind it
+        # in the copy queue and the steps run one after another: 15.7-18.3 us
+        # per step against 12.9 us staged.)
 
         def e2e_run(n):
-            for i in range(min(LOOKAHEAD, n)):
-                stage(i)
+            for i in range(min(nbuf, n)):
+                set_stream(e2e_streams[i])
+                darenas[i].copy_(harena[i % NUM_POOLS], non_blocking=True)
             for i in range(n):
-                if i + LOOKAHEAD < n:
-                    stage(i + LOOKAHEAD)
                 bb = i % nbuf
                 set_stream(e2e_streams[bb])
                 dq, dbt, dsl = dviews[bb]
                 k, v = kv[i % NUM_POOLS]
                 decode_into(dq, k, v, dbt, dsl, douts[bb])
                 hout_rows[i % e2e_steps].copy_(douts[bb], non_blocking=True)
+                if i + nbuf < n:
+                    darenas[bb].copy_(harena[(i + nbuf) % NUM_POOLS], non_blocking=True)
 
         # Warm-up of 2 x E2E_STEPS untimed steps: a fresh process's first few
         # thousand steps of this loop run 15-17 us per step before settling at
@@ -382,7 +381,8 @@ def _run_ours(args, rank, world, torch, dist, device, clocks):
             "api": "flashdec_b200.paged_decode_attention_into; q, block tables and seq_lens in one "
                    "pinned host arena, one H2D and one D2H copy per step; steps rotate over "
                    "four streams with their own device buffers and workspaces, each step's "
-                   "inputs staged three steps ahead",
+                   "inputs copied in three steps ahead of its kernel (after the D2H of the "
+                   "step four back, on the same stream)",
             "check": f"all {e2e_steps} host outputs equal the device-resident decode of their inputs",
             "timing": "wall clock between device-wide synchronisations",
         }
