@@ -1038,7 +1038,15 @@ def _pool_init(kind, workload):
 
         torch.set_num_threads(1)
         sys.path.insert(0, str(REF_DIR))
+        # the repository's own ``flashdec`` (an alias of flashdec_b200) must
+        # not stand in for the reference: drop it if anything imported it
+        for name in [m for m in sys.modules if m == "flashdec" or m.startswith("flashdec.")]:
+            del sys.modules[name]
+        import flashdec.paged_reference as ref_mod
         from flashdec.paged_reference import paged_decode_attention_ref
+
+        if not Path(ref_mod.__file__).resolve().is_relative_to(REF_DIR.resolve()):
+            raise RuntimeError(f"reference arm imported {ref_mod.__file__}, not the reference")
 
         q, k, v, bt, sl = arrays
         dt = torch.float32 if workload == "c1" else torch.bfloat16

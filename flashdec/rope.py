@@ -1,0 +1,6 @@
+"""``flashdec.rope``: the same module object as :mod:`flashdec_b200.rope`."""
+
+import importlib
+import sys
+
+sys.modules[__name__] = importlib.import_module("flashdec_b200.rope")

@@ -46,6 +46,8 @@ def _install_package(tmp_path: Path) -> Path:
     shutil.copy(ROOT / "pyproject.toml", src / "pyproject.toml")
     shutil.copytree(ROOT / "flashdec_b200", src / "flashdec_b200",
                     ignore=shutil.ignore_patterns("__pycache__", "_build", "csrc"))
+    shutil.copytree(ROOT / "flashdec", src / "flashdec",
+                    ignore=shutil.ignore_patterns("__pycache__"))
     site = tmp_path / "site"
     subprocess.run([sys.executable, "-m", "pip", "install", "--quiet", "--no-index",
                     "--no-deps", "--no-build-isolation", "--target", str(site), str(src)],
