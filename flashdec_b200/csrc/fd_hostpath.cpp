@@ -20,6 +20,9 @@
 //    shape checks, the output allocation and one fd_paged_decode (or
 //    fd_cascade_decode) on the current stream.
 //
+//  * vllm_into / register_vllm: the same for the vLLM launcher
+//    (_vllm_paged_decode_attention_into) with the auto plan.
+//
 //  * staging_wait / staging_copy / unpack_meta: the engine's per-token
 //    metadata upload (one copy from a reused pinned slot, one event per slot)
 //    and its split into typed views, each one call instead of several torch
@@ -192,6 +195,113 @@ py::object layer_run(int64_t args, int64_t cascade, const at::Tensor& q, const a
   return py::cast(out);
 }
 
+// ---- the vLLM launcher (kernels/paged_decode.py _vllm_paged_decode_attention_into)
+// Same scheme as decode_into for the launcher's eight tensors (q, append_k,
+// append_v, the 5-D kv_cache, block tables, seq_lens, out, slot_mapping)
+// and its scalars; a hit sets the pointers (V's plane is kv_cache plus one
+// stride of its K/V axis) and launches.  The caller keeps the registered
+// struct's workspace alive.
+constexpr int kVllmTensors = 8;
+constexpr int kVllmRank = 5;
+
+struct VllmSignature {
+  std::array<int64_t, kVllmTensors * (2 + 2 * kVllmRank) + 7> v{};
+  bool operator==(const VllmSignature& o) const { return v == o.v; }
+};
+
+struct VllmSignatureHash {
+  size_t operator()(const VllmSignature& s) const {
+    uint64_t h = 1469598103934665603ull;
+    for (int64_t x : s.v) h ^= static_cast<uint64_t>(x) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    return static_cast<size_t>(h);
+  }
+};
+
+std::unordered_map<VllmSignature, fd_paged_decode_args, VllmSignatureHash> g_vllm;
+
+bool vllm_signature(const at::Tensor* const* ts, cudaStream_t stream, int64_t num_reqs,
+                    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                    int64_t block_size, double sm_scale, VllmSignature* s) {
+  int j = 0;
+  for (int i = 0; i < kVllmTensors; ++i) {
+    const at::Tensor& t = *ts[i];
+    const int64_t r = t.dim();
+    if (r > kVllmRank || !t.is_cuda()) return false;
+    s->v[j++] = r;
+    s->v[j++] = static_cast<int64_t>(t.scalar_type()) * 1024 + t.get_device();
+    const auto sz = t.sizes();
+    const auto st = t.strides();
+    for (int64_t d = 0; d < kVllmRank; ++d) {
+      s->v[j++] = d < r ? sz[d] : 0;
+      s->v[j++] = d < r ? st[d] : 0;
+    }
+  }
+  int64_t scale_bits;
+  std::memcpy(&scale_bits, &sm_scale, sizeof(scale_bits));
+  s->v[j++] = num_reqs;
+  s->v[j++] = num_q_heads;
+  s->v[j++] = num_kv_heads;
+  s->v[j++] = head_dim;
+  s->v[j++] = block_size;
+  s->v[j++] = scale_bits;
+  s->v[j] = reinterpret_cast<int64_t>(stream);
+  return true;
+}
+
+int vllm_into(const at::Tensor& q, const at::Tensor& append_k, const at::Tensor& append_v,
+              const at::Tensor& kv_cache, const at::Tensor& block_tables,
+              const at::Tensor& seq_lens, const at::Tensor& out, const at::Tensor& slot_mapping,
+              int64_t num_reqs, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+              int64_t block_size, double sm_scale) {
+  if (!g_decode || g_vllm.empty()) return kMiss;
+  cudaStream_t stream;
+  if (!current_stream_of(q, &stream)) return kMiss;
+  const at::Tensor* ts[kVllmTensors] = {&q, &append_k, &append_v, &kv_cache,
+                                        &block_tables, &seq_lens, &out, &slot_mapping};
+  VllmSignature s;
+  if (!vllm_signature(ts, stream, num_reqs, num_q_heads, num_kv_heads, head_dim, block_size,
+                      sm_scale, &s))
+    return kMiss;
+  auto it = g_vllm.find(s);
+  if (it == g_vllm.end()) return kMiss;
+  fd_paged_decode_args& a = it->second;
+  char* kv = static_cast<char*>(kv_cache.data_ptr());
+  a.q = q.data_ptr();
+  a.out = out.data_ptr();
+  a.k_cache = kv;
+  a.v_cache = kv + kv_cache.stride(1) * kv_cache.element_size();
+  a.append_k = append_k.data_ptr();
+  a.append_v = append_v.data_ptr();
+  a.block_tables = block_tables.data_ptr();
+  a.seq_lens = seq_lens.data_ptr();
+  a.slot_mapping = slot_mapping.data_ptr();
+  return g_decode(&a, stream);
+}
+
+bool register_vllm(const at::Tensor& q, const at::Tensor& append_k, const at::Tensor& append_v,
+                   const at::Tensor& kv_cache, const at::Tensor& block_tables,
+                   const at::Tensor& seq_lens, const at::Tensor& out,
+                   const at::Tensor& slot_mapping, int64_t num_reqs, int64_t num_q_heads,
+                   int64_t num_kv_heads, int64_t head_dim, int64_t block_size, double sm_scale,
+                   int64_t args) {
+  cudaStream_t stream;
+  if (!current_stream_of(q, &stream)) return false;
+  if (kv_cache.dim() != 5 || kv_cache.size(1) != 2) return false;
+  const at::Tensor* ts[kVllmTensors] = {&q, &append_k, &append_v, &kv_cache,
+                                        &block_tables, &seq_lens, &out, &slot_mapping};
+  VllmSignature s;
+  if (!vllm_signature(ts, stream, num_reqs, num_q_heads, num_kv_heads, head_dim, block_size,
+                      sm_scale, &s))
+    return false;
+  if (g_vllm.size() >= kTableLimit) g_vllm.clear();
+  fd_paged_decode_args copy;
+  std::memcpy(&copy, reinterpret_cast<const void*>(args), sizeof(copy));
+  g_vllm[s] = copy;
+  return true;
+}
+
+void clear_vllm() { g_vllm.clear(); }
+
 // ---- pinned staging of the engine's per-token metadata -------------------
 // One event per slot of a Python-owned pinned ring (flashdec_b200.cache):
 // staging_wait blocks until the slot's previous copy has completed,
@@ -272,6 +382,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clear", &clear);
   m.def("table_size", &table_size);
   m.def("layer_run", &layer_run);
+  m.def("vllm_into", &vllm_into);
+  m.def("register_vllm", &register_vllm);
+  m.def("clear_vllm", &clear_vllm);
   m.def("staging_wait", &staging_wait);
   m.def("staging_copy", &staging_copy);
   m.def("staging_release", &staging_release);

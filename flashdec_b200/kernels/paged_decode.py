@@ -75,6 +75,19 @@ def _fast_entry():
     return _FAST
 
 
+# prepared vLLM launches registered with the C++ host path (kept alive with
+# the per-stream workspaces their structs point at)
+_VLLM_PREPARED: list = []
+_VLLM_FAST = None
+
+
+def _vllm_fast_entry():
+    global _VLLM_FAST
+    hp = _lib.load_hostpath()
+    _VLLM_FAST = (hp.vllm_into, hp.MISS)
+    return _VLLM_FAST
+
+
 def _register(prep, q, k_cache, v_cache, block_tables, seq_lens, out):
     """Hand the struct that just launched (bound to the current stream's
     workspace, which ``prep`` keeps alive while it is in ``_PREPARED``) to
@@ -414,9 +427,37 @@ def _vllm_paged_decode_attention_into(
     using vLLM's ``softmax_segm_*`` buffers as the split workspace, followed
     by the reducer (``MASK_INVALID_SLOT`` semantics).
     """
+    # the auto plan (num_splits 0, vLLM's default here) goes to the C++ host
+    # path first: a signature it has seen on this stream only sets pointers
+    if num_splits == 0:
+        decode, miss = _VLLM_FAST or _vllm_fast_entry()
+        try:
+            rc = decode(q, append_k, append_v, kv_cache, block_tables, seq_lens, out,
+                        slot_mapping, num_reqs, num_q_heads, num_kv_heads, head_dim,
+                        block_size, float(sm_scale))
+        except TypeError:
+            rc = miss
+        if rc == 0:
+            return out
+        if rc < 0:
+            _lib.check(rc, "fd_paged_decode")
     k4 = kv_cache[:, 0].permute(0, 2, 1, 3)
     v4 = kv_cache[:, 1].permute(0, 2, 1, 3)
     fused = dict(append_k=append_k, append_v=append_v, slot_mapping=slot_mapping)
+    if num_splits == 0:
+        prep = _native.prepare_paged_decode(
+            q, k4, v4, block_tables, seq_lens, out, sm_scale=sm_scale, block_size=block_size,
+            num_seqs=num_reqs, num_splits=0, **fused)
+        prep.launch(q, k4, v4, block_tables, seq_lens, out, _native.stream_handle(q.device))
+        hp = _lib.load_hostpath()
+        if len(_VLLM_PREPARED) >= _PREPARED_LIMIT:
+            _VLLM_PREPARED.clear()
+            hp.clear_vllm()  # its entries use the dropped workspaces
+        if hp.register_vllm(q, append_k, append_v, kv_cache, block_tables, seq_lens, out,
+                            slot_mapping, num_reqs, num_q_heads, num_kv_heads, head_dim,
+                            block_size, float(sm_scale), ctypes.addressof(prep.args)):
+            _VLLM_PREPARED.append(prep)
+        return out
     if num_splits >= 2:
         acc = split_acc[:, :, :num_splits, :]
         mx = split_max[:, :, :num_splits]
