@@ -2235,6 +2235,7 @@ constexpr int kSplitMaxTilesPerCta = 32;
 constexpr int kSplitMinTilesPerCta = 2;
 constexpr int kWaveSplitCap = 14;
 constexpr int kWaveBalancedMaxTiles = 64;
+constexpr int kWaveFillCap = 12;
 
 // FLASHDEC_B200_BALANCED_MAX_TILES=n: a batch takes the balanced split plan
 // while pairs x tiles <= SMs x n (tuning sweeps; default kSplitMaxTilesPerCta)
@@ -2279,8 +2280,16 @@ Plan make_plan(const fd_paged_decode_args& a, const Derived& dv, const DeviceInf
       // more, about 1.3 CTAs per SM beat one (measured over B1-B16,
       // contexts 1k-8k).
       s = std::min<int64_t>(s, kWaveSplitCap);
-      if (pl.cap_tiles >= kWaveLongTiles * s)
+      if (pl.cap_tiles >= kWaveLongTiles * s) {
         s = std::max<int64_t>(s, std::min<int64_t>(kWaveSplitCap, nsm * 13 / 10 / pairs));
+        // Splits that still hold 16 tiles or more go up to one full wave at
+        // two CTAs per SM (clusters of at most 12, whose co-residency holds
+        // at 16 pairs): B16 x 5120 tokens 21.9 -> 18.8 us, the c5 layer 15.1
+        // -> 13.3 us; fewer tiles per split (B16 x 2048) keep the rule above.
+        const int64_t fill = std::min<int64_t>(
+            {kWaveFillCap, 2 * nsm / pairs, static_cast<int64_t>(pl.cap_tiles) / 16});
+        s = std::max<int64_t>(s, fill);
+      }
       if (wave_splits_override() > 0) s = wave_splits_override();
     }
     s = std::max<int64_t>(1, s);
