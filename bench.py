@@ -1,6 +1,7 @@
 """Benchmark of the B200 paged-decode attention (BASELINE.json metric).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --vllm-e2e [--eager]
 
 Workload (N = 1): BASELINE config 2 -- Qwen2.5-3B decode attention, B=8,
 16 query / 2 KV heads, head_dim 128, block_size 32, context 2048, bf16, KV
@@ -22,6 +23,11 @@ sharded across the N ranks by length-balanced (LPT) request sharding.
 reference installed under baseline/_ref; the numpy oracle restating it when
 that install is absent) on the same workload, on all host cores, on rank 0
 only.
+
+``--vllm-e2e`` (opt-in, a few minutes, one GPU) times vLLM's own
+``LLM.generate`` on the Qwen2.5-3B architecture with dummy weights, once with
+vLLM's TRITON_ATTN backend and once with this package's CUSTOM backend, and
+prints their decode step times and greedy-token agreement as one JSON line.
 """
 
 from __future__ import annotations
@@ -1175,6 +1181,107 @@ def run_reference(args, rank, world):
     }
 
 
+# Qwen2.5-3B's architecture (public model config); weights are vLLM's dummy
+# initialisation, so no checkpoint is needed
+QWEN25_3B = {
+    "architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2", "hidden_size": 2048,
+    "intermediate_size": 11008, "num_hidden_layers": 36, "num_attention_heads": 16,
+    "num_key_value_heads": 2, "max_position_embeddings": 32768, "rope_theta": 1000000.0,
+    "rms_norm_eps": 1e-06, "vocab_size": 151936, "tie_word_embeddings": True,
+    "torch_dtype": "bfloat16", "hidden_act": "silu", "use_sliding_window": False,
+    "max_window_layers": 36, "bos_token_id": 151643, "eos_token_id": 151643,
+}
+VLLM_E2E = dict(batch=8, prompt=2048, decode=128)
+
+
+def run_vllm_e2e(eager):
+    """Opt-in (--vllm-e2e): vLLM ``LLM.generate`` on the Qwen2.5-3B
+    architecture (dummy weights), B8 prompts of 2048 tokens, 128 greedy decode
+    tokens each, once with vLLM's TRITON_ATTN backend and once with this
+    package's CUSTOM backend, each in its own process.  Decode throughput is
+    the difference between a 129-token and a 1-token generation of the same
+    prompts (so prefill is taken out)."""
+    import tempfile
+
+    res = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        model = Path(tmp) / "model"
+        model.mkdir()
+        (model / "config.json").write_text(json.dumps(QWEN25_3B))
+        for backend in ("TRITON_ATTN", "CUSTOM"):
+            out = Path(tmp) / f"{backend}.json"
+            cmd = [sys.executable, str(Path(__file__).resolve()), "--vllm-e2e-worker", backend,
+                   str(out), str(model)] + (["--eager"] if eager else [])
+            subprocess.run(cmd, cwd=REPO, check=True, timeout=1800)
+            res[backend] = json.loads(out.read_text())
+    t, c = res["TRITON_ATTN"], res["CUSTOM"]
+    tt, ct = t.pop("tokens"), c.pop("tokens")
+    # greedy tokens of the two backends (bf16 attention rounding can flip a
+    # near-tie, after which a sequence diverges): first-token agreement and
+    # the share of positions equal up to each sequence's first difference
+    first = sum(a[0] == b[0] for a, b in zip(tt, ct)) / len(tt)
+    prefix = []
+    for a, b in zip(tt, ct):
+        n = next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
+        prefix.append(n / len(a))
+    return {"vllm_e2e": "Qwen2.5-3B architecture, dummy weights, B8 x 2048-token prompts, 128 greedy "
+                        "decode tokens, vLLM LLM.generate",
+            "cuda_graphs": not eager, "triton_attn": t, "custom": c,
+            "decode_speedup": t["decode_ms_per_step"] / c["decode_ms_per_step"],
+            "greedy_first_token_agreement": first,
+            "greedy_common_prefix_mean": sum(prefix) / len(prefix)}
+
+
+def _vllm_e2e_worker(backend, out_path, model_dir, eager):
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")  # engine core in-process
+    import numpy as np
+
+    calls = {"n": 0}
+    if backend == "CUSTOM":
+        import flashdec_b200.vllm_backend as vb
+        from flashdec_b200 import vllm_plugin
+
+        vllm_plugin.register()
+        orig = vb._vllm_paged_decode_attention_into
+
+        def counted(*a, **k):
+            calls["n"] += 1
+            return orig(*a, **k)
+
+        vb._vllm_paged_decode_attention_into = counted
+    from vllm import LLM, SamplingParams
+    from vllm.inputs import TokensPrompt
+
+    cfg = VLLM_E2E
+    llm = LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
+              max_model_len=cfg["prompt"] + cfg["decode"] + 64, gpu_memory_utilization=0.5,
+              attention_backend=backend, seed=0, enforce_eager=eager,
+              max_num_seqs=cfg["batch"])
+    rng = np.random.default_rng(0)
+    prompts = [TokensPrompt(prompt_token_ids=[int(x) for x in rng.integers(100, 150000, cfg["prompt"])])
+               for _ in range(cfg["batch"])]
+
+    tokens = []
+
+    def timed(n):
+        sp = SamplingParams(max_tokens=n, temperature=0.0, ignore_eos=True, detokenize=False)
+        t0 = time.perf_counter()
+        outs = llm.generate(prompts, sp, use_tqdm=False)
+        dt = time.perf_counter() - t0
+        assert all(len(o.outputs[0].token_ids) == n for o in outs)
+        tokens[:] = [list(o.outputs[0].token_ids) for o in outs]
+        return dt
+
+    timed(4)  # warm-up
+    t1 = min(timed(1) for _ in range(3))
+    tn = min(timed(cfg["decode"] + 1) for _ in range(3))
+    step_ms = (tn - t1) * 1000.0 / cfg["decode"]
+    Path(out_path).write_text(json.dumps({
+        "backend": backend, "prefill_s": t1, "generate_s": tn, "decode_ms_per_step": step_ms,
+        "decode_tokens_per_s": cfg["batch"] / (step_ms / 1000.0),
+        "flashdec_launcher_calls": calls["n"], "tokens": tokens}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1191,7 +1298,18 @@ def main():
                          "batch, 1.5 GB of KV), c5 (one layer of the c5 shape, plain decode) or "
                          "vllm (the vLLM launcher at B8 ctx2048 with the fused append); "
                          "the small cases used for ncu captures")
+    ap.add_argument("--vllm-e2e", action="store_true",
+                    help="opt-in: vLLM LLM.generate decode throughput on the Qwen2.5-3B "
+                         "architecture (dummy weights), TRITON_ATTN against CUSTOM; minutes")
+    ap.add_argument("--eager", action="store_true", help="with --vllm-e2e: no CUDA graphs")
+    ap.add_argument("--vllm-e2e-worker", nargs=3, default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.vllm_e2e_worker:
+        _vllm_e2e_worker(*args.vllm_e2e_worker, eager=args.eager)
+        return
+    if args.vllm_e2e:
+        print(json.dumps(run_vllm_e2e(args.eager)), flush=True)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
