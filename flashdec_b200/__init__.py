@@ -29,6 +29,7 @@ __all__ = [
     "rope_paged_kv_append",
     "device_status",
     "reserve_workspace",
+    "copy_async",
 ]
 
 __version__ = "0.2.0"
@@ -74,6 +75,12 @@ def _resolve(name):
             "paged_decode_attention": paged_decode.paged_decode_attention,
             "paged_decode_attention_into": paged_decode.paged_decode_attention_into,
         }[name]
+    if name == "copy_async":
+        # the C++ function itself: one cudaMemcpyAsync per call, no Python
+        # frame in between (a missing host-path module raises here)
+        from ._lib import load_hostpath
+
+        return load_hostpath().copy_async
     if name == "device_status":
         from ._lib import device_status
 

@@ -28,6 +28,10 @@
 //    and its split into typed views, each one call instead of several torch
 //    operations.
 //
+//  * copy_async(dst, src): the public flashdec_b200.copy_async, one
+//    stream-ordered cudaMemcpyAsync between a host tensor and a device
+//    tensor (or two device tensors) on the device's current stream.
+//
 // The entry points are taken as addresses from the already-loaded
 // libflashdec_b200.so (set_entry_points), so both paths call the same
 // library.  Every function runs with the GIL held, which serialises the
@@ -372,6 +376,37 @@ std::vector<at::Tensor> unpack_meta(const at::Tensor& buf, int64_t n) {
 
 }  // namespace
 
+// copy_async(dst, src): dst <- src, bytes as stored, on the current stream of
+// the CUDA side's device.  Unlike Tensor.copy_(non_blocking=True) nothing is
+// recorded for the host allocator: the caller keeps both tensors alive (and
+// the host side unchanged) until the stream has passed the copy.  A pageable
+// host tensor makes the copy synchronous with the host, as cudaMemcpyAsync
+// does.  Misuse raises ValueError before any CUDA call.
+void copy_async(const at::Tensor& dst, const at::Tensor& src) {
+  if (!dst.defined() || !src.defined()) throw py::value_error("copy_async: undefined tensor");
+  const bool dc = dst.is_cuda();
+  const bool sc = src.is_cuda();
+  if (!dc && !sc) throw py::value_error("copy_async: one of dst and src must be a CUDA tensor");
+  if ((!dc && !dst.is_cpu()) || (!sc && !src.is_cpu()))
+    throw py::value_error("copy_async: tensors must be on the CPU or a CUDA device");
+  if (!dst.is_contiguous() || !src.is_contiguous())
+    throw py::value_error("copy_async: dst and src must be contiguous");
+  const int64_t nbytes = dst.numel() * static_cast<int64_t>(dst.element_size());
+  if (nbytes != src.numel() * static_cast<int64_t>(src.element_size()))
+    throw py::value_error("copy_async: dst and src must hold the same number of bytes");
+  const int dev = c10::cuda::current_device();
+  if ((dc && dst.get_device() != dev) || (sc && src.get_device() != dev))
+    throw py::value_error("copy_async: CUDA tensors must be on the current CUDA device");
+  if (nbytes == 0) return;
+  const cudaMemcpyKind kind = dc && sc ? cudaMemcpyDeviceToDevice
+                              : dc     ? cudaMemcpyHostToDevice
+                                       : cudaMemcpyDeviceToHost;
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  const cudaError_t e = cudaMemcpyAsync(dst.data_ptr(), src.data_ptr(), static_cast<size_t>(nbytes),
+                                        kind, stream);
+  if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "C++ host path of the prepared flashdec_b200 launches";
   m.attr("MISS") = kMiss;
@@ -389,4 +424,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("staging_copy", &staging_copy);
   m.def("staging_release", &staging_release);
   m.def("unpack_meta", &unpack_meta);
+  m.def("copy_async", &copy_async, py::arg("dst"), py::arg("src"),
+        "dst <- src on the current stream of the CUDA side's device (one cudaMemcpyAsync); "
+        "keep both tensors alive until the stream has passed the copy");
 }

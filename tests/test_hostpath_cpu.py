@@ -74,3 +74,16 @@ def test_layer_run_rejects_shapes_with_the_engine_messages(hp):
         hp.layer_run(addr, 0, q, k[:, :1], k, 0, 0)
     with pytest.raises(ValueError, match="current CUDA device"):
         hp.layer_run(addr, 0, q, k, k, 0, 0)
+
+
+def test_copy_async_rejects_misuse_before_any_cuda_call(hp):
+    import flashdec_b200
+
+    assert flashdec_b200.copy_async is hp.copy_async
+    a = torch.zeros(8)
+    with pytest.raises(ValueError, match="one of dst and src must be a CUDA tensor"):
+        hp.copy_async(a, torch.ones(8))
+    with pytest.raises(ValueError, match="one of dst and src must be a CUDA tensor"):
+        hp.copy_async(a[::2], torch.ones(4))
+    with pytest.raises(TypeError):
+        hp.copy_async(a, None)
