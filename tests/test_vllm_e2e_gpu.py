@@ -8,9 +8,11 @@ in-tree package stays first on ``PYTHONPATH`` so the in-tree sm_100a library
 is the one loaded.  A tiny Qwen2-shaped model (16 q heads / 2 KV heads,
 head_dim 128, dummy weights) generates greedily from prompts of 520-1200
 tokens once with vLLM's Triton backend and once with CUSTOM; tokens and top
-logprobs must agree and the B200 decode kernel must actually have run.
+logprobs must agree and the B200 decode kernel must actually have run.  The
+pair runs twice: eager, and in vLLM's default CUDA-graph mode, where the
+decode batches replay FULL graphs whose capture recorded the B200 kernel.
 
-Runs by default under ``-m gpu`` (two vLLM start-ups, a few minutes);
+Runs by default under ``-m gpu`` (four vLLM start-ups, a few minutes);
 FD_SKIP_VLLM_E2E=1 skips it."""
 
 from __future__ import annotations
@@ -59,28 +61,39 @@ def _install_package(tmp_path: Path) -> Path:
     return site
 
 
-@pytest.mark.skipif(os.environ.get("FD_SKIP_VLLM_E2E") == "1", reason="FD_SKIP_VLLM_E2E=1")
-def test_custom_backend_matches_vllm_triton(tmp_path):
+@pytest.fixture(scope="module")
+def installed(tmp_path_factory):
+    if os.environ.get("FD_SKIP_VLLM_E2E") == "1":
+        pytest.skip("FD_SKIP_VLLM_E2E=1")
     pytest.importorskip("vllm")
-    site = _install_package(tmp_path)
-    model = tmp_path / "model"
+    tmp = tmp_path_factory.mktemp("vllm_e2e")
+    site = _install_package(tmp)
+    model = tmp / "model"
     model.mkdir()
     (model / "config.json").write_text(json.dumps(CONFIG))
+    return tmp, site, model
+
+
+@pytest.mark.parametrize("mode", ["eager", "graph"])
+def test_custom_backend_matches_vllm_triton(installed, mode):
+    tmp, site, model = installed
     env = dict(os.environ, FD_MODEL_DIR=str(model),
                PYTHONPATH=os.pathsep.join([str(ROOT), str(site),
                                            os.environ.get("PYTHONPATH", "")]))
     results, seconds = {}, {}
     for backend in ("TRITON_ATTN", "CUSTOM"):
-        out = tmp_path / f"{backend}.json"
+        out = tmp / f"{backend}_{mode}.json"
         t0 = time.monotonic()
-        subprocess.run([sys.executable, "-m", "tests.vllm_e2e_worker", backend, str(out)],
+        subprocess.run([sys.executable, "-m", "tests.vllm_e2e_worker", backend, str(out), mode],
                        cwd=ROOT, env=env, check=True, timeout=900)
         seconds[backend] = time.monotonic() - t0
         results[backend] = json.loads(out.read_text())
-    print(f"vLLM e2e wall seconds: {seconds}")
+    print(f"vLLM e2e ({mode}) wall seconds: {seconds}")
     ref, ours = results["TRITON_ATTN"], results["CUSTOM"]
     assert ours["plugin_loaded"], "vLLM did not load flashdec_b200 through its entry point"
     assert ours["flashdec_launches"] > 0, "the CUSTOM backend never reached the B200 kernel"
+    if mode == "graph":
+        assert ours["flashdec_captured_launches"] > 0, "no FULL graph recorded the B200 kernel"
     assert [o["tokens"] for o in ours["outputs"]] == [o["tokens"] for o in ref["outputs"]]
     for a, b in zip(ref["outputs"], ours["outputs"]):
         for la, lb in zip(a["logprobs"], b["logprobs"]):
