@@ -381,7 +381,8 @@ std::vector<at::Tensor> unpack_meta(const at::Tensor& buf, int64_t n) {
 // recorded for the host allocator: the caller keeps both tensors alive (and
 // the host side unchanged) until the stream has passed the copy.  A pageable
 // host tensor makes the copy synchronous with the host, as cudaMemcpyAsync
-// does.  Misuse raises ValueError before any CUDA call.
+// does.  Misuse (sizes, layout, devices, overlapping device ranges) raises
+// ValueError before any CUDA call.
 void copy_async(const at::Tensor& dst, const at::Tensor& src) {
   if (!dst.defined() || !src.defined()) throw py::value_error("copy_async: undefined tensor");
   const bool dc = dst.is_cuda();
@@ -398,6 +399,12 @@ void copy_async(const at::Tensor& dst, const at::Tensor& src) {
   if ((dc && dst.get_device() != dev) || (sc && src.get_device() != dev))
     throw py::value_error("copy_async: CUDA tensors must be on the current CUDA device");
   if (nbytes == 0) return;
+  if (dc && sc) {
+    const auto d0 = reinterpret_cast<uintptr_t>(dst.data_ptr());
+    const auto s0 = reinterpret_cast<uintptr_t>(src.data_ptr());
+    if (d0 < s0 + static_cast<uintptr_t>(nbytes) && s0 < d0 + static_cast<uintptr_t>(nbytes))
+      throw py::value_error("copy_async: dst and src overlap");
+  }
   const cudaMemcpyKind kind = dc && sc ? cudaMemcpyDeviceToDevice
                               : dc     ? cudaMemcpyHostToDevice
                                        : cudaMemcpyDeviceToHost;

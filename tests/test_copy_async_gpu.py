@@ -1,8 +1,8 @@
 """flashdec_b200.copy_async on the GPU: pinned host -> device, device ->
 pinned host and device -> device copies of the bytes as stored (any dtype
 pair of equal size), in order with the kernels of the current stream, and
-the reference-style ValueErrors for mismatched sizes, non-contiguous tensors
-and a CUDA tensor off the current device."""
+ValueErrors for mismatched sizes, non-contiguous tensors, overlapping device
+ranges and a CUDA tensor off the current device."""
 
 from __future__ import annotations
 
@@ -71,4 +71,8 @@ def test_misuse_raises_value_error():
     if torch.cuda.device_count() > 1:
         with pytest.raises(ValueError, match="current CUDA device"):
             flashdec_b200.copy_async(torch.zeros(8, device="cuda:1"), torch.zeros(8))
+    buf = torch.zeros(16, device="cuda")
+    with pytest.raises(ValueError, match="overlap"):
+        flashdec_b200.copy_async(buf[4:12], buf[:8])
+    flashdec_b200.copy_async(buf[8:], buf[:8])  # adjacent ranges are fine
     flashdec_b200.copy_async(torch.empty(0, device="cuda"), torch.empty(0))  # nothing to copy
