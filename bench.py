@@ -1218,20 +1218,30 @@ def run_vllm_e2e(eager):
             res[backend] = json.loads(out.read_text())
     t, c = res["TRITON_ATTN"], res["CUSTOM"]
     tt, ct = t.pop("tokens"), c.pop("tokens")
-    # greedy tokens of the two backends (bf16 attention rounding can flip a
-    # near-tie, after which a sequence diverges): first-token agreement and
-    # the share of positions equal up to each sequence's first difference
-    first = sum(a[0] == b[0] for a, b in zip(tt, ct)) / len(tt)
-    prefix = []
-    for a, b in zip(tt, ct):
-        n = next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
-        prefix.append(n / len(a))
+    first, prefix = greedy_agreement(tt, ct)
     return {"vllm_e2e": "Qwen2.5-3B architecture, dummy weights, B8 x 2048-token prompts, 128 greedy "
                         "decode tokens, vLLM LLM.generate",
             "cuda_graphs": not eager, "triton_attn": t, "custom": c,
             "decode_speedup": t["decode_ms_per_step"] / c["decode_ms_per_step"],
             "greedy_first_token_agreement": first,
-            "greedy_common_prefix_mean": sum(prefix) / len(prefix)}
+            "greedy_common_prefix_mean": prefix}
+
+
+def greedy_agreement(ref_tokens, our_tokens):
+    """Greedy token sequences of two backends on the same prompts -> (share
+    of sequences whose first token agrees, mean share of each sequence equal
+    up to its first difference).  bf16 attention rounding can flip a near-tie,
+    after which a greedy sequence diverges, so the common prefix, not the
+    count of equal positions, is the measure."""
+    if len(ref_tokens) != len(our_tokens) or not ref_tokens:
+        raise ValueError("need the same, non-zero number of sequences from both backends")
+    first = sum(bool(a) and bool(b) and a[0] == b[0]
+                for a, b in zip(ref_tokens, our_tokens)) / len(ref_tokens)
+    prefix = []
+    for a, b in zip(ref_tokens, our_tokens):
+        n = next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), min(len(a), len(b)))
+        prefix.append(n / max(len(a), len(b), 1))
+    return first, sum(prefix) / len(prefix)
 
 
 def _vllm_e2e_worker(backend, out_path, model_dir, eager):
